@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the CacheBridge online handoff hot path on B200.
+
+Metric: mapped+installed KV tokens/s, plus p50 handoff latency
+at an 8K-token history. One "step" is one handoff: every token of the history
+is gathered from the source pool, mapped by the CacheBridge mapper (40 -> 64
+layers, 8 KV heads, S=2) and installed into the target pool rows of its page
+table.
+
+  N=1  (default)  BASELINE config 2: one 8192-token request, page_size=1 pools
+                  of 262144 slots, seeded random source and target slot lists.
+  N>1  (torchrun) BASELINE config 3 (and its TP2 / TP1 variants): source TP
+                  N/2 + target TP N/2; rank r < N/2 maps its heads for 16 x
+                  32768-token requests and stores them straight into the peer
+                  target rank's pool (CUDA IPC pointers, NVLink), in
+                  double-buffered 2048-token chunks; the prefix is published
+                  after an all-rank vote.
+  --impl reference  the reference algorithm on the host CPU (the oracle
+                  restatement of src/cachebridge/mapper.py map_page + pool
+                  install), on the same config.
+
+All inputs are synthetic and seeded; mapper weights are random-init (bf16
+values), source KV ~ N(0,1) x per-channel LogNormal(0, 0.5) with keys stored
+RoPE-applied. Inputs are larger than L2 (1.3 GB read + 2.1 GB written per
+step), so no L2 flush is needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "mapped+installed KV tokens/s; p50 handoff latency at 8K-token history"
+UNIT = "tokens/s"
+
+# BASELINE config 2 (Qwen3-14B -> Qwen3-32B shapes)
+QWEN = dict(L_s=40, L_t=64, H=8, D=128, S=2, theta=1e6)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ----------------------------------------------------------------------------
+# synthetic workload
+# ----------------------------------------------------------------------------
+def random_layers(*, L_s, L_t, H, D, S, seed):
+    """Seeded headwise mapper layers: S distinct source layers per target layer,
+    W ~ N(0, 1/(S*D)) and b ~ N(0, 0.01), rounded to bf16 values (stored FP32)."""
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for _ in range(L_t):
+        sel = torch.randperm(L_s, generator=g)[:S]
+        t = dict(selected=sel.long(), headwise=torch.tensor(True))
+        for kind in ("k", "v"):
+            t[f"{kind}_weight"] = (torch.randn(H, S * D, D, generator=g) / math.sqrt(S * D)).bfloat16().float()
+            t[f"{kind}_bias"] = (torch.randn(H, D, generator=g) * 0.1).bfloat16().float()
+        layers.append(t)
+    return layers
+
+
+def fill_source_rows(pool, slots, *, positions, theta, seed, device):
+    """Write a synthetic RoPE-applied history into pool rows `slots`."""
+    from cachebridge_b200.rope import rope_parameters
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, D = pool.heads, pool.head_dim
+    inv, mag = rope_parameters(D, theta)
+    inv = torch.from_numpy(inv).to(device)
+    phase = positions.to(device).float()[:, None] * inv[None, :]
+    cos, sin = (phase.cos() * mag)[:, None, :], (phase.sin() * mag)[:, None, :]
+    n = len(slots)
+    chunk = 4096
+    for l in range(pool.layer_num):
+        scale_k = torch.exp(0.5 * torch.randn(1, H, D, generator=g, device=device))
+        scale_v = torch.exp(0.5 * torch.randn(1, H, D, generator=g, device=device))
+        for a in range(0, n, chunk):
+            b = min(n, a + chunk)
+            k = torch.randn(b - a, H, D, generator=g, device=device) * scale_k
+            v = torch.randn(b - a, H, D, generator=g, device=device) * scale_v
+            x0, x1 = k[..., : D // 2], k[..., D // 2 :]
+            c, s = cos[a:b], sin[a:b]
+            k = torch.cat((x0 * c - x1 * s, x1 * c + x0 * s), dim=-1)
+            pool.k_buffer[l][slots[a:b]] = k.to(pool.dtype)
+            pool.v_buffer[l][slots[a:b]] = v.to(pool.dtype)
+
+
+def algorithmic_work(*, n, L_t, H, D, S, used, idx_bytes=8):
+    """Per-handoff algorithmic bytes and flops (source rows read once, target rows
+    written once, weights once, two slot tables)."""
+    bytes_ = n * (2 * used * H * D * 2 + 2 * L_t * H * D * 2) + 2 * L_t * H * (S * D * D + D) * 2 + 2 * n * idx_bytes
+    flops = 4 * L_t * H * S * D * D * n
+    return bytes_, flops
+
+
+def measured_peaks():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic(name):
+    p = ROOT / "profiles" / f"{name}.json"
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=self.out, stderr=subprocess.DEVNULL,
+            )
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        busy = [r for r in rows if r["power"] > 300] or rows
+        reasons = sorted({name for r in busy for name, key in
+                          (("hw_slowdown", "hw"), ("hw_thermal_slowdown", "hwt"),
+                           ("sw_thermal_slowdown", "swt"), ("sw_power_cap", "pcap"))
+                          if r[key].lower() == "active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in busy), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": reasons, "samples": len(busy), "power_w_max": max(r["power"] for r in rows)}
+
+
+# ----------------------------------------------------------------------------
+# CPU reference (oracle restatement of the reference's torch CPU path)
+# ----------------------------------------------------------------------------
+def cpu_reference_tokens_per_s(layers, *, n_sample, reps, seed=7):
+    """Time the reference algorithm (map_page + SGLang-style install) on the host."""
+    from oracle import mapper_oracle as orc
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    L_s, H, D = QWEN["L_s"], QWEN["H"], QWEN["D"]
+    page = (torch.randn(2, L_s, n_sample, H, D, generator=g)).bfloat16()
+    head_range = (0, H)
+    ref_layers = [dict(selected=t["selected"].tolist(), k_weight=t["k_weight"], k_bias=t["k_bias"],
+                       v_weight=t["v_weight"], v_bias=t["v_bias"]) for t in layers]
+    L_t = len(ref_layers)
+    pool_k = [torch.zeros(2 * n_sample, H, D, dtype=torch.bfloat16) for _ in range(L_t)]
+    pool_v = [torch.zeros(2 * n_sample, H, D, dtype=torch.bfloat16) for _ in range(L_t)]
+    loc = torch.randperm(2 * n_sample, generator=g)[:n_sample]
+    times = []
+    for r in range(reps + 1):
+        t0 = time.perf_counter()
+        out = orc.map_page(ref_layers, page, position_start=r * n_sample, head_range=head_range,
+                           source_theta=QWEN["theta"], target_theta=QWEN["theta"])
+        orc.install(pool_k, pool_v, loc, out)
+        times.append(time.perf_counter() - t0)
+    best = statistics.median(times[1:]) if reps else times[0]
+    return n_sample / best, torch.get_num_threads()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    layers = random_layers(L_s=QWEN["L_s"], L_t=QWEN["L_t"], H=QWEN["H"], D=QWEN["D"], S=QWEN["S"], seed=11)
+    n_sample = args.ref_tokens
+    from oracle import mapper_oracle as orc  # noqa: F401  (the timed CPU implementation)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(3)
+    L_s, H, D = QWEN["L_s"], QWEN["H"], QWEN["D"]
+    page = torch.randn(2, L_s, n_sample, H, D, generator=g).bfloat16()
+    ref_layers = [dict(selected=t["selected"].tolist(), k_weight=t["k_weight"], k_bias=t["k_bias"],
+                       v_weight=t["v_weight"], v_bias=t["v_bias"]) for t in layers]
+    pool_k = [torch.zeros(2 * n_sample, H, D, dtype=torch.bfloat16) for _ in range(len(ref_layers))]
+    pool_v = [torch.zeros(2 * n_sample, H, D, dtype=torch.bfloat16) for _ in range(len(ref_layers))]
+    loc = torch.randperm(2 * n_sample, generator=g)[:n_sample]
+
+    def step(i):
+        out = orc.map_page(ref_layers, page, position_start=(i * n_sample) % 8192, head_range=(0, H),
+                           source_theta=QWEN["theta"], target_theta=QWEN["theta"])
+        orc.install(pool_k, pool_v, loc, out)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    times = []
+    for i in range(args.steps):
+        s0 = time.perf_counter()
+        step(i)
+        times.append(time.perf_counter() - s0)
+    elapsed = time.perf_counter() - t0
+    value = n_sample * args.steps / elapsed
+    cores = torch.get_num_threads()
+    line = dict(
+        impl="reference", metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps,
+        warmup=args.warmup, ms_per_step=1e3 * elapsed / args.steps, higher_is_better=True,
+        scaling="weak" if args.gpus == 1 else "strong", vs_baseline=None, dtype="f32", data="synthetic",
+        config=dict(workload="qwen3-14b->32b handoff (BASELINE config 2), CPU sample", tokens_per_step=n_sample,
+                    source_layers=L_s, target_layers=QWEN["L_t"], kv_heads=H, head_dim=D, selected=QWEN["S"]),
+        cpu_baseline=dict(value=value, unit=UNIT, cores=cores, kind="port",
+                          sample=f"{n_sample} of the 8192 history tokens per step (one reference block), "
+                                 "all 40->64 layers and 8 heads, FP32 torch on host cores"),
+        e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+        latency_p50_ms=1e3 * statistics.median(times),
+    )
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------
+# N = 1
+# ----------------------------------------------------------------------------
+def run_single(args):
+    import cachebridge_b200 as cb
+    from cachebridge_b200.online.blocks import map_write_block
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, rows = args.tokens, args.pool_slots
+    L_s, L_t, H, D, S, theta = (QWEN[k] for k in ("L_s", "L_t", "H", "D", "S", "theta"))
+    layers = random_layers(L_s=L_s, L_t=L_t, H=H, D=D, S=S, seed=11)
+    mapper = cb.PageMapper.from_tensors(layers, method="cachebridge", source_rope_theta=theta,
+                                        target_rope_theta=theta, device=dev)
+    used = len({int(x) for t in layers for x in t["selected"]})
+    g = torch.Generator().manual_seed(5)
+    src_slots = torch.randperm(rows, generator=g)[:n].to(dev)
+    dst_slots = torch.randperm(rows, generator=g)[:n].to(dev)
+    log(f"allocating pools: source {L_s}x{rows} rows, target {L_t}x{rows} rows")
+    src_pool = cb.TokenKVPool(layers=L_s, rows=rows, heads=H, head_dim=D, device=dev, fill=0.0)
+    dst_pool = cb.TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=dev)
+    fill_source_rows(src_pool, src_slots, positions=torch.arange(n), theta=theta, seed=9, device=dev)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        call = mapper.prepare(src_pool.rows(src_slots), dst_pool.rows(dst_slots), n, position_start=0)
+    launches_per_step = 3  # rope table + key derotation/pack + fused map/install
+    bytes_alg, flops = algorithmic_work(n=n, L_t=L_t, H=H, D=D, S=S, used=used)
+
+    def step():
+        call.refresh_tables()
+        call.derotate()
+        call.install()
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    stream.synchronize()
+    cb.raise_for_status(dev)
+
+    # ---- device-resident timing (value, latency, per-kernel) -----------------
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for k in range(args.steps):
+                ev[k][0].record(stream)
+                call.refresh_tables()
+                call.derotate()
+                ev[k][1].record(stream)
+                call.install()
+                ev[k][2].record(stream)
+            end.record(stream)
+        end.synchronize()
+    cb.raise_for_status(dev)
+    total_ms = start.elapsed_time(end)
+    step_ms = [ev[k][0].elapsed_time(ev[k][2]) for k in range(args.steps)]
+    tc_ms = [ev[k][1].elapsed_time(ev[k][2]) for k in range(args.steps)]
+    pre_ms = [ev[k][0].elapsed_time(ev[k][1]) for k in range(args.steps)]
+    value = n * args.steps / (total_ms / 1e3)
+
+    # ---- end to end through the public API, host buffers ---------------------
+    block_host = torch.empty((2, L_s, n, H, D), dtype=torch.bfloat16).pin_memory()
+    for l in range(L_s):  # the history as a packed source block (pack_source_block layout)
+        block_host[0, l].copy_(src_pool.k_buffer[l][src_slots].cpu())
+        block_host[1, l].copy_(src_pool.v_buffer[l][src_slots].cpu())
+    idx_host = dst_slots.cpu().pin_memory()
+    status_host = torch.empty(1, dtype=torch.int32).pin_memory()
+    block_dev = torch.empty_like(block_host, device=dev)
+    idx_dev = torch.empty_like(idx_host, device=dev)
+    status = cb.device.status_word(dev)
+
+    def e2e_step():
+        block_dev.copy_(block_host, non_blocking=True)
+        idx_dev.copy_(idx_host, non_blocking=True)
+        map_write_block(mapper, block_dev, dst_pool, idx_dev, start=0, source_head_offset=0)
+        status_host.copy_(status, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    stream.synchronize()
+    e2e_times = []
+    with torch.cuda.stream(stream):
+        for _ in range(args.e2e_steps):
+            t0 = time.perf_counter()
+            e2e_step()
+            stream.synchronize()
+            if int(status_host.item()):
+                raise RuntimeError(f"device status {int(status_host.item())}")
+            e2e_times.append(time.perf_counter() - t0)
+    e2e_value = n / statistics.mean(e2e_times)
+    h2d = block_host.numel() * 2 + idx_host.numel() * 8
+    del block_dev, block_host
+
+    # ---- CPU baseline (reference algorithm on host cores, bounded sample) -------
+    cpu_value, cores = cpu_reference_tokens_per_s(layers, n_sample=args.cpu_tokens, reps=2)
+
+    hbm_peak, tc_peak, peak_kind = measured_peaks()
+    tc_avg_s = statistics.mean(tc_ms) / 1e3
+    achieved = bytes_alg / tc_avg_s / 1e9
+    traffic = profiled_traffic("map_install_tc_cfg2_traffic")
+    line = dict(
+        metric=METRIC, value=value, unit=UNIT, n_gpus=1, steps=args.steps, warmup=args.warmup,
+        ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
+        dtype="bf16", data="synthetic",
+        config=dict(workload="qwen3-14b->32b single-GPU handoff (BASELINE config 2)", history_tokens=n,
+                    source_layers=L_s, target_layers=L_t, kv_heads=H, head_dim=D, selected=S,
+                    pool_slots=rows, page_size=1, slot_lists="seeded random", l2="inputs larger than L2",
+                    parallelism="single GPU (source and target pools on one device)"),
+        latency_p50_ms=statistics.median(step_ms),
+        roofline=dict(bound="hbm", achieved=achieved, peak=hbm_peak, unit="GB/s", frac=achieved / hbm_peak,
+                      traffic=None if traffic is None else traffic.get("dram_bytes_per_launch"),
+                      kernel="map_install_tc_kernel", algorithmic_bytes=bytes_alg, peak_source=peak_kind,
+                      tensor_tflops=flops / tc_avg_s / 1e12, tensor_frac=flops / tc_avg_s / 1e12 / tc_peak),
+        kernels_ms=dict(map_install_tc=statistics.mean(tc_ms), rope_table_and_derotate=statistics.mean(pre_ms)),
+        cpu_baseline=dict(value=cpu_value, unit=UNIT, cores=cores, kind="port",
+                          sample=f"{args.cpu_tokens}-token block of the same workload (40->64 layers, 8 heads), "
+                                 "reference torch algorithm restated in oracle/, FP32 on host cores"),
+        e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=4,
+                 path="map_write_block(pinned host source block -> device, install into the target pool)",
+                 latency_p50_ms=1e3 * statistics.median(e2e_times)),
+        gpu_launches=launches_per_step * args.steps,
+        clocks=clocks.summary(),
+    )
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=8192, help="history tokens (N=1)")
+    ap.add_argument("--pool-slots", type=int, default=262144)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-tokens", type=int, default=2048)
+    ap.add_argument("--ref-tokens", type=int, default=2048)
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        log("warm-up raised to 3 steps (timing rule)")
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        return run_single(args)
+    from cachebridge_b200.tp_bench import run_sharded
+
+    return run_sharded(args, METRIC, UNIT, QWEN)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,620 @@
+// Host implementation of the C ABI declared in include/cachebridge_b200.h.
+//
+// Validates every request on the host (geometry, alignment, layer counts),
+// packs kernel parameter blocks and launches on the caller's stream. Hot-path
+// entry points allocate nothing; cb_mapper_create owns all device memory of a
+// mapper. Errors are reported by status code plus a thread-local message.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/cachebridge_b200.h"
+#include "cb_kernels.cuh"
+#include "cb_map_tc.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return static_cast<uint16_t>((u >> 16) | 0x40);
+  const uint32_t rounding = 0x7FFFu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>((u + rounding) >> 16);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int elem_size(int dtype) { return dtype == CB_DTYPE_F32 ? 4 : 2; }
+
+int check_rows(const cb_rows* r, const char* name, int head_dim, int heads_used, int dtype,
+               bool need_16b) {
+  if (r == nullptr) return fail(CB_ERR_INVALID, std::string(name) + ": null row set");
+  if (r->layers <= 0 || r->layers > CB_MAX_LAYERS)
+    return fail(CB_ERR_UNSUPPORTED, std::string(name) + ": layers must be in [1, 128]");
+  if (r->k == nullptr || r->v == nullptr) return fail(CB_ERR_INVALID, std::string(name) + ": null layer arrays");
+  if (r->heads <= 0 || r->head_offset < 0 || r->head_offset + heads_used > r->heads)
+    return fail(CB_ERR_INVALID, std::string(name) + ": head range outside the row");
+  if (r->row_stride < static_cast<int64_t>(r->heads) * head_dim)
+    return fail(CB_ERR_INVALID, std::string(name) + ": row_stride smaller than a row");
+  if (r->rows <= 0) return fail(CB_ERR_INVALID, std::string(name) + ": rows must be positive");
+  if (r->slot_dtype != CB_INDEX_NONE && r->slot_dtype != CB_INDEX_I32 && r->slot_dtype != CB_INDEX_I64)
+    return fail(CB_ERR_INVALID, std::string(name) + ": unknown slot dtype");
+  if (r->slot_dtype != CB_INDEX_NONE && r->slots == nullptr)
+    return fail(CB_ERR_INVALID, std::string(name) + ": slot dtype given without slots");
+  const int es = elem_size(dtype);
+  for (int l = 0; l < r->layers; ++l) {
+    if (r->k[l] == nullptr || r->v[l] == nullptr)
+      return fail(CB_ERR_INVALID, std::string(name) + ": null layer pointer");
+    if (reinterpret_cast<uintptr_t>(r->k[l]) % es || reinterpret_cast<uintptr_t>(r->v[l]) % es)
+      return fail(CB_ERR_INVALID, std::string(name) + ": layer pointer not element aligned");
+    if (need_16b && (!aligned16(r->k[l]) || !aligned16(r->v[l])))
+      return fail(CB_ERR_INVALID, std::string(name) + ": layer pointer not 16-byte aligned");
+  }
+  if (need_16b && (r->row_stride * es) % 16 != 0)
+    return fail(CB_ERR_INVALID, std::string(name) + ": row stride not a multiple of 16 bytes");
+  return CB_OK;
+}
+
+std::once_flag g_tc_attr_once[64];
+
+}  // namespace
+
+struct cb_mapper {
+  int device = 0;
+  int L_t = 0, H = 0, D = 0, S = 0, U = 0;
+  int num_sms = 0;
+  int max_sel = 0;
+  std::vector<int> used;  // sorted unique selected source layers
+  float* w32 = nullptr;   // [2][L_t][H][S*D][D]
+  float* b32 = nullptr;   // [2][L_t][H][D]
+  int* sel = nullptr;     // [L_t][S]
+  int* sel_local = nullptr;
+  int* used_dev = nullptr;
+  uint8_t* w_img = nullptr;  // head_dim 128 only: [2][L_t][H][S][32 KB]
+};
+
+namespace {
+
+int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
+                    size_t workspace_bytes, const float* cos, const float* sin);
+
+int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int64_t n_tokens,
+                    const float* src_cos, const float* src_sin, void* workspace, int32_t* dev_status) {
+  cbk::DerotateParams dp{};
+  dp.n_tokens = n_tokens;
+  dp.H = m->H;
+  dp.U = m->U;
+  for (int l = 0; l < src->layers; ++l) dp.src_k[l] = src->k[l];
+  dp.used = m->used_dev;
+  dp.src_row_stride = src->row_stride;
+  dp.src_rows = src->rows;
+  dp.src_head_offset = src->head_offset;
+  dp.src_slot_dtype = src->slot_dtype;
+  dp.src_slots = src->slots;
+  dp.scos = src_cos;
+  dp.ssin = src_sin;
+  dp.ws = static_cast<__nv_bfloat16*>(workspace);
+  dp.status = dev_status;
+  const int blocks = static_cast<int>((n_tokens + 7) / 8);
+  cbk::derotate_pack_kernel<<<blocks, 256, 0, st>>>(dp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "derotate_pack launch");
+  return CB_OK;
+}
+
+int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst,
+              int64_t n_tokens, const float* dst_cos, const float* dst_sin, const void* workspace,
+              int32_t* dev_status) {
+  cbk::MapTcParams p{};
+  p.n_tokens = static_cast<int>(n_tokens);
+  p.L_t = m->L_t;
+  p.H = m->H;
+  p.S = m->S;
+  p.R = 4;
+  p.n_chunks = static_cast<int>((n_tokens + p.R * cbk::kBM - 1) / (p.R * cbk::kBM));
+  const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
+  if (items > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "work too large for one call");
+  p.num_items = static_cast<int>(items);
+  p.w_resident = m->S <= 4;
+  p.w_slots = p.w_resident ? m->S : 2;
+  const int stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(p.w_slots, 0)) / cbk::kKBlockBytes;
+  p.stages = std::min(stages, 4);
+  if (p.stages < 2) return fail(CB_ERR_UNSUPPORTED, "shared memory too small for the pipeline");
+  p.w_img = m->w_img;
+  p.bias = m->b32;
+  p.sel_global = m->sel;
+  p.sel_local = m->sel_local;
+  p.ws_k = static_cast<const __nv_bfloat16*>(workspace);
+  for (int l = 0; l < src->layers; ++l) p.src_v[l] = src->v[l];
+  p.src_row_stride = src->row_stride;
+  p.src_rows = src->rows;
+  p.src_head_offset = src->head_offset;
+  p.src_slot_dtype = src->slot_dtype;
+  p.src_slots = src->slots;
+  for (int l = 0; l < dst->layers; ++l) {
+    p.dst_k[l] = dst->k[l];
+    p.dst_v[l] = dst->v[l];
+  }
+  p.dst_row_stride = dst->row_stride;
+  p.dst_rows = dst->rows;
+  p.dst_head_offset = dst->head_offset;
+  p.dst_slot_dtype = dst->slot_dtype;
+  p.dst_slots = dst->slots;
+  p.dcos = dst_cos;
+  p.dsin = dst_sin;
+  p.status = dev_status;
+  const int smem = cbk::tc_smem_bytes(p.w_slots, p.stages);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(g_tc_attr_once[m->device & 63], [&] {
+    attr_err = cudaFuncSetAttribute(cbk::map_install_tc_kernel,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cbk::kTcMaxSmem);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  const int grid = static_cast<int>(std::min<int64_t>(items, m->num_sms));
+  cbk::map_install_tc_kernel<<<grid, cbk::kTcThreads, smem, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "map_install_tc launch");
+  return CB_OK;
+}
+
+int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
+                    size_t workspace_bytes, const float* cos, const float* sin) {
+  const size_t need = static_cast<size_t>(m->U) * static_cast<size_t>(n_tokens) * m->H * cbk::kD * 2;
+  if (m->D != cbk::kD || dtype != CB_DTYPE_BF16)
+    return fail(CB_ERR_UNSUPPORTED, "tensor-core path needs head_dim 128 and bf16 storage");
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return fail(CB_ERR_INVALID, "workspace missing, too small or misaligned");
+  if (cos == nullptr || sin == nullptr) return fail(CB_ERR_INVALID, "null RoPE table");
+  if (!aligned16(cos) || !aligned16(sin)) return fail(CB_ERR_INVALID, "RoPE tables must be 16-byte aligned");
+  return CB_OK;
+}
+
+// Shared validation of a tensor-core call's row sets.
+int check_tc_call(const cb_mapper* m, const cb_rows* src, const cb_rows* dst, int64_t n_tokens) {
+  if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
+  if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
+  if (n_tokens > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "too many tokens in one call");
+  int rc = check_rows(src, "src", m->D, m->H, CB_DTYPE_BF16, true);
+  if (rc != CB_OK) return rc;
+  if (src->layers <= m->max_sel) return fail(CB_ERR_INVALID, "mapper selected layer exceeds source page depth");
+  if (dst != nullptr) {
+    if ((rc = check_rows(dst, "dst", m->D, m->H, CB_DTYPE_BF16, true)) != CB_OK) return rc;
+    if (dst->layers != m->L_t) return fail(CB_ERR_INVALID, "destination layer count != mapper target layers");
+  }
+  return CB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cb_version(void) { return 100; }
+
+const char* cb_status_string(int status) {
+  switch (status) {
+    case CB_OK: return "ok";
+    case CB_ERR_INVALID: return "invalid argument or geometry";
+    case CB_ERR_UNSUPPORTED: return "unsupported geometry";
+    case CB_ERR_CUDA: return "CUDA runtime error";
+    case CB_ERR_ALIAS: return "destination rows alias";
+    default: return "unknown status";
+  }
+}
+
+const char* cb_last_error(void) { return g_last_error.c_str(); }
+
+int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, int head_dim,
+                     int num_selected, const int64_t* selected, const float* k_weight,
+                     const float* k_bias, const float* v_weight, const float* v_bias) {
+  if (out == nullptr) return fail(CB_ERR_INVALID, "null output handle");
+  *out = nullptr;
+  if (target_layers <= 0 || target_layers > CB_MAX_LAYERS)
+    return fail(CB_ERR_UNSUPPORTED, "target_layers must be in [1, 128]");
+  if (heads <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 256)
+    return fail(CB_ERR_INVALID, "heads must be positive and head_dim even and <= 256");
+  if (num_selected <= 0 || num_selected > 16) return fail(CB_ERR_UNSUPPORTED, "num_selected must be in [1, 16]");
+  if (!selected || !k_weight || !k_bias || !v_weight || !v_bias)
+    return fail(CB_ERR_INVALID, "null mapper tensor");
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return fail(CB_ERR_INVALID, "device index out of range");
+
+  auto* m = new cb_mapper();
+  m->device = device;
+  m->L_t = target_layers;
+  m->H = heads;
+  m->D = head_dim;
+  m->S = num_selected;
+  std::vector<int> sel(static_cast<size_t>(target_layers) * num_selected);
+  for (size_t i = 0; i < sel.size(); ++i) {
+    if (selected[i] < 0 || selected[i] >= CB_MAX_LAYERS) {
+      delete m;
+      return fail(CB_ERR_INVALID, "selected source layer outside [0, 128)");
+    }
+    sel[i] = static_cast<int>(selected[i]);
+    m->max_sel = std::max(m->max_sel, sel[i]);
+  }
+  m->used = sel;
+  std::sort(m->used.begin(), m->used.end());
+  m->used.erase(std::unique(m->used.begin(), m->used.end()), m->used.end());
+  m->U = static_cast<int>(m->used.size());
+  std::vector<int> sel_local(sel.size());
+  for (size_t i = 0; i < sel.size(); ++i)
+    sel_local[i] = static_cast<int>(std::lower_bound(m->used.begin(), m->used.end(), sel[i]) - m->used.begin());
+
+  const int F = num_selected * head_dim;
+  const size_t w_per_kind = static_cast<size_t>(target_layers) * heads * F * head_dim;
+  const size_t b_per_kind = static_cast<size_t>(target_layers) * heads * head_dim;
+
+  DeviceGuard guard(device);
+  if (!guard.ok) {
+    delete m;
+    return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  }
+  cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device);
+
+  auto cleanup = [&](cudaError_t err, const char* what) {
+    cb_mapper_destroy(m);
+    return cuda_fail(err, what);
+  };
+  if ((e = cudaMalloc(&m->w32, 2 * w_per_kind * sizeof(float))) != cudaSuccess) return cleanup(e, "cudaMalloc w32");
+  if ((e = cudaMalloc(&m->b32, 2 * b_per_kind * sizeof(float))) != cudaSuccess) return cleanup(e, "cudaMalloc b32");
+  if ((e = cudaMalloc(&m->sel, sel.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc sel");
+  if ((e = cudaMalloc(&m->sel_local, sel.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc sel_local");
+  if ((e = cudaMalloc(&m->used_dev, m->used.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc used");
+  if ((e = cudaMemcpy(m->w32, k_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload k_weight");
+  if ((e = cudaMemcpy(m->w32 + w_per_kind, v_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload v_weight");
+  if ((e = cudaMemcpy(m->b32, k_bias, b_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload k_bias");
+  if ((e = cudaMemcpy(m->b32 + b_per_kind, v_bias, b_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload v_bias");
+  if ((e = cudaMemcpy(m->sel, sel.data(), sel.size() * sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload sel");
+  if ((e = cudaMemcpy(m->sel_local, sel_local.data(), sel.size() * sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload sel_local");
+  if ((e = cudaMemcpy(m->used_dev, m->used.data(), m->used.size() * sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload used");
+
+  if (head_dim == cbk::kD) {
+    // Tensor-core image: for each (kind, layer, head, k-block j) a 32 KB block
+    // holding W^T (rows = output dim d, K-major = input feature) as two
+    // 128B-swizzled panels of 64 features; 16-byte chunk c of row d sits at
+    // chunk position c ^ (d & 7) of its 128-byte row.
+    const size_t units = 2ull * target_layers * heads;
+    std::vector<uint16_t> img(units * num_selected * (cbk::kKBlockBytes / 2));
+    for (int kind = 0; kind < 2; ++kind) {
+      const float* W = kind ? v_weight : k_weight;
+      for (int l = 0; l < target_layers; ++l)
+        for (int h = 0; h < heads; ++h) {
+          const float* wh = W + (static_cast<size_t>(l) * heads + h) * F * head_dim;
+          const size_t unit = (static_cast<size_t>(kind) * target_layers + l) * heads + h;
+          for (int j = 0; j < num_selected; ++j) {
+            uint16_t* blk = img.data() + (unit * num_selected + j) * (cbk::kKBlockBytes / 2);
+            for (int f = 0; f < 128; ++f) {
+              const int panel = f >> 6, chunk = (f & 63) >> 3, e8 = f & 7;
+              const float* wrow = wh + static_cast<size_t>(j * 128 + f) * head_dim;
+              for (int d = 0; d < 128; ++d) {
+                const size_t byte = static_cast<size_t>(panel) * cbk::kPanelBytes + d * 128 +
+                                    ((chunk ^ (d & 7)) << 4) + e8 * 2;
+                blk[byte / 2] = f32_to_bf16_rne(wrow[d]);
+              }
+            }
+          }
+        }
+    }
+    if ((e = cudaMalloc(&m->w_img, img.size() * sizeof(uint16_t))) != cudaSuccess) return cleanup(e, "cudaMalloc w_img");
+    if ((e = cudaMemcpy(m->w_img, img.data(), img.size() * sizeof(uint16_t), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload w_img");
+  }
+  *out = m;
+  return CB_OK;
+}
+
+int cb_mapper_destroy(cb_mapper* m) {
+  if (m == nullptr) return CB_OK;
+  DeviceGuard guard(m->device);
+  cudaFree(m->w32);
+  cudaFree(m->b32);
+  cudaFree(m->sel);
+  cudaFree(m->sel_local);
+  cudaFree(m->used_dev);
+  cudaFree(m->w_img);
+  delete m;
+  return CB_OK;
+}
+
+int cb_mapper_info(const cb_mapper* m, int* target_layers, int* heads, int* head_dim,
+                   int* num_selected, int* used_source_layers) {
+  if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
+  if (target_layers) *target_layers = m->L_t;
+  if (heads) *heads = m->H;
+  if (head_dim) *head_dim = m->D;
+  if (num_selected) *num_selected = m->S;
+  if (used_source_layers) *used_source_layers = m->U;
+  return CB_OK;
+}
+
+size_t cb_mapper_workspace_bytes(const cb_mapper* m, int dtype, int64_t n_tokens) {
+  if (m == nullptr || n_tokens <= 0) return 0;
+  if (m->D != cbk::kD || dtype != CB_DTYPE_BF16) return 0;
+  return static_cast<size_t>(m->U) * static_cast<size_t>(n_tokens) * m->H * cbk::kD * 2;
+}
+
+int cb_rope_table(void* stream, const float* inv_freq, int half_dim, float magnitude,
+                  int64_t position_start, int64_t n, float* out_cos, float* out_sin) {
+  if (inv_freq == nullptr || half_dim <= 0 || half_dim > 128 || n < 0 || position_start < 0)
+    return fail(CB_ERR_INVALID, "rope table: bad arguments");
+  if (n == 0) return CB_OK;
+  if (out_cos == nullptr || out_sin == nullptr) return fail(CB_ERR_INVALID, "rope table: null output");
+  cbk::RopeTableParams p{};
+  std::memcpy(p.inv_freq, inv_freq, sizeof(float) * half_dim);
+  p.half_dim = half_dim;
+  p.magnitude = magnitude;
+  p.position_start = position_start;
+  p.n = n;
+  p.out_cos = out_cos;
+  p.out_sin = out_sin;
+  const int64_t total = n * half_dim;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 65535));
+  cbk::rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope_table launch");
+  return CB_OK;
+}
+
+int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
+                   int64_t n_tokens, const float* src_cos, const float* src_sin,
+                   const float* dst_cos, const float* dst_sin, int dtype, void* workspace,
+                   size_t workspace_bytes, int32_t* dev_status) {
+  if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
+  if (dtype != CB_DTYPE_BF16 && dtype != CB_DTYPE_F32) return fail(CB_ERR_UNSUPPORTED, "dtype must be bf16 or fp32");
+  if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
+  if (n_tokens > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "too many tokens in one call");
+  const bool tc = (m->D == cbk::kD && dtype == CB_DTYPE_BF16);
+  int rc;
+  if ((rc = check_rows(src, "src", m->D, m->H, dtype, tc)) != CB_OK) return rc;
+  if ((rc = check_rows(dst, "dst", m->D, m->H, dtype, tc)) != CB_OK) return rc;
+  if (src->layers <= m->max_sel) return fail(CB_ERR_INVALID, "mapper selected layer exceeds source page depth");
+  if (dst->layers != m->L_t) return fail(CB_ERR_INVALID, "destination layer count != mapper target layers");
+  if (n_tokens == 0) return CB_OK;
+  if (!src_cos || !src_sin || !dst_cos || !dst_sin) return fail(CB_ERR_INVALID, "null RoPE table");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DeviceGuard guard(m->device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+
+  if (tc) {
+    if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes, src_cos, src_sin)) != CB_OK) return rc;
+    if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes, dst_cos, dst_sin)) != CB_OK) return rc;
+    if ((rc = launch_derotate(m, st, src, n_tokens, src_cos, src_sin, workspace, dev_status)) != CB_OK) return rc;
+    return launch_tc(m, st, src, dst, n_tokens, dst_cos, dst_sin, workspace, dev_status);
+  }
+
+  // Generic CUDA-core path.
+  cbk::SimtParams p{};
+  p.L_t = m->L_t;
+  p.H = m->H;
+  p.S = m->S;
+  p.D = m->D;
+  p.w32 = m->w32;
+  p.b32 = m->b32;
+  p.sel = m->sel;
+  for (int l = 0; l < src->layers; ++l) {
+    p.src_k[l] = src->k[l];
+    p.src_v[l] = src->v[l];
+  }
+  p.src_row_stride = src->row_stride;
+  p.src_rows = src->rows;
+  p.src_head_offset = src->head_offset;
+  p.src_slot_dtype = src->slot_dtype;
+  p.src_slots = src->slots;
+  for (int l = 0; l < dst->layers; ++l) {
+    p.dst_k[l] = dst->k[l];
+    p.dst_v[l] = dst->v[l];
+  }
+  p.dst_row_stride = dst->row_stride;
+  p.dst_rows = dst->rows;
+  p.dst_head_offset = dst->head_offset;
+  p.dst_slot_dtype = dst->slot_dtype;
+  p.dst_slots = dst->slots;
+  p.scos = src_cos;
+  p.ssin = src_sin;
+  p.dcos = dst_cos;
+  p.dsin = dst_sin;
+  p.status = dev_status;
+  const size_t smem = static_cast<size_t>(m->H) * (m->S * m->D + m->D) * sizeof(float);
+  if (smem > static_cast<size_t>(cbk::kTcMaxSmem)) return fail(CB_ERR_UNSUPPORTED, "generic mapper: heads*features too large");
+  if (n_tokens > 2147483647ll) return fail(CB_ERR_UNSUPPORTED, "too many tokens");
+  dim3 grid(static_cast<unsigned>(n_tokens), static_cast<unsigned>(m->L_t), 2);
+  cudaError_t e = cbk::launch_map_simt(dtype == CB_DTYPE_F32, p, grid, smem, st);
+  if (e != cudaSuccess) return cuda_fail(e, "map_install_simt launch");
+  return CB_OK;
+}
+
+int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_tokens,
+                     const float* src_cos, const float* src_sin, void* workspace,
+                     size_t workspace_bytes, int32_t* dev_status) {
+  int rc = check_tc_call(m, src, nullptr, n_tokens);
+  if (rc != CB_OK) return rc;
+  if (n_tokens == 0) return CB_OK;
+  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes, src_cos, src_sin)) != CB_OK)
+    return rc;
+  DeviceGuard guard(m->device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, src_cos, src_sin, workspace,
+                         dev_status);
+}
+
+int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
+                          int64_t n_tokens, const float* dst_cos, const float* dst_sin,
+                          const void* workspace, size_t workspace_bytes, int32_t* dev_status) {
+  int rc = check_tc_call(m, src, dst, n_tokens);
+  if (rc != CB_OK) return rc;
+  if (n_tokens == 0) return CB_OK;
+  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes, dst_cos, dst_sin)) != CB_OK)
+    return rc;
+  DeviceGuard guard(m->device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, dst_cos, dst_sin, workspace,
+                   dev_status);
+}
+
+static int launch_copy_rows(cudaStream_t st, cbk::CopyRowsParams& p, int64_t n) {
+  if (n == 0) return CB_OK;
+  int vec = 16;
+  auto ok_for = [&](int v) {
+    if (p.row_bytes % v) return false;
+    if (p.src_stride_bytes % v || p.dst_stride_bytes % v || p.src_offset_bytes % v || p.dst_offset_bytes % v) return false;
+    for (int l = 0; l < p.layers; ++l) {
+      if (reinterpret_cast<uintptr_t>(p.src_k[l]) % v || reinterpret_cast<uintptr_t>(p.src_v[l]) % v) return false;
+      if (reinterpret_cast<uintptr_t>(p.dst_k[l]) % v || reinterpret_cast<uintptr_t>(p.dst_v[l]) % v) return false;
+    }
+    return true;
+  };
+  while (vec > 2 && !ok_for(vec)) vec >>= 1;
+  if (!ok_for(vec)) return fail(CB_ERR_INVALID, "row copy: rows not 2-byte aligned");
+  const int64_t rows = 2 * static_cast<int64_t>(p.layers) * n;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows + 7) / 8, 148 * 32));
+  cudaError_t e = cbk::launch_copy_rows(vec, p, blocks, st);
+  if (e != cudaSuccess) return cuda_fail(e, "copy_rows launch");
+  return CB_OK;
+}
+
+int cb_pack_rows(void* stream, const cb_rows* src, int head_dim, int dtype, int64_t n_tokens,
+                 void* out, int32_t* dev_status) {
+  if (dtype != CB_DTYPE_BF16 && dtype != CB_DTYPE_F32) return fail(CB_ERR_UNSUPPORTED, "dtype must be bf16 or fp32");
+  if (head_dim <= 0) return fail(CB_ERR_INVALID, "head_dim must be positive");
+  if (src == nullptr) return fail(CB_ERR_INVALID, "null row set");
+  const int heads = src->heads - src->head_offset;
+  int rc = check_rows(src, "src", head_dim, heads, dtype, false);
+  if (rc != CB_OK) return rc;
+  if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
+  if (n_tokens > 0 && out == nullptr) return fail(CB_ERR_INVALID, "null output block");
+  const int es = elem_size(dtype);
+  cbk::CopyRowsParams p{};
+  p.layers = src->layers;
+  p.row_bytes = heads * head_dim * es;
+  p.n = n_tokens;
+  for (int l = 0; l < src->layers; ++l) {
+    p.src_k[l] = src->k[l];
+    p.src_v[l] = src->v[l];
+    p.dst_k[l] = static_cast<char*>(out) + (static_cast<int64_t>(l) * n_tokens) * p.row_bytes;
+    p.dst_v[l] = static_cast<char*>(out) + (static_cast<int64_t>(src->layers + l) * n_tokens) * p.row_bytes;
+  }
+  p.src_stride_bytes = src->row_stride * es;
+  p.src_offset_bytes = static_cast<int64_t>(src->head_offset) * head_dim * es;
+  p.src_rows = src->rows;
+  p.src_slot_dtype = src->slot_dtype;
+  p.src_slots = src->slots;
+  p.dst_stride_bytes = p.row_bytes;
+  p.dst_offset_bytes = 0;
+  p.dst_rows = n_tokens;
+  p.dst_slot_dtype = CB_INDEX_NONE;
+  p.dst_slots = nullptr;
+  p.status = dev_status;
+  return launch_copy_rows(static_cast<cudaStream_t>(stream), p, n_tokens);
+}
+
+int cb_install_rows(void* stream, const void* block, const cb_rows* dst, int head_dim, int dtype,
+                    int64_t n_tokens, int32_t* dev_status) {
+  if (dtype != CB_DTYPE_BF16 && dtype != CB_DTYPE_F32) return fail(CB_ERR_UNSUPPORTED, "dtype must be bf16 or fp32");
+  if (head_dim <= 0) return fail(CB_ERR_INVALID, "head_dim must be positive");
+  if (dst == nullptr) return fail(CB_ERR_INVALID, "null row set");
+  const int heads = dst->heads - dst->head_offset;
+  int rc = check_rows(dst, "dst", head_dim, heads, dtype, false);
+  if (rc != CB_OK) return rc;
+  if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
+  if (n_tokens > 0 && block == nullptr) return fail(CB_ERR_INVALID, "null source block");
+  const int es = elem_size(dtype);
+  cbk::CopyRowsParams p{};
+  p.layers = dst->layers;
+  p.row_bytes = heads * head_dim * es;
+  p.n = n_tokens;
+  for (int l = 0; l < dst->layers; ++l) {
+    p.src_k[l] = static_cast<const char*>(block) + (static_cast<int64_t>(l) * n_tokens) * p.row_bytes;
+    p.src_v[l] = static_cast<const char*>(block) + (static_cast<int64_t>(dst->layers + l) * n_tokens) * p.row_bytes;
+    p.dst_k[l] = dst->k[l];
+    p.dst_v[l] = dst->v[l];
+  }
+  p.src_stride_bytes = p.row_bytes;
+  p.src_offset_bytes = 0;
+  p.src_rows = n_tokens;
+  p.src_slot_dtype = CB_INDEX_NONE;
+  p.src_slots = nullptr;
+  p.dst_stride_bytes = dst->row_stride * es;
+  p.dst_offset_bytes = static_cast<int64_t>(dst->head_offset) * head_dim * es;
+  p.dst_rows = dst->rows;
+  p.dst_slot_dtype = dst->slot_dtype;
+  p.dst_slots = dst->slots;
+  p.status = dev_status;
+  return launch_copy_rows(static_cast<cudaStream_t>(stream), p, n_tokens);
+}
+
+int cb_ipc_export(const void* device_ptr, void* handle_out) {
+  if (device_ptr == nullptr || handle_out == nullptr) return fail(CB_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, 64);
+  return CB_OK;
+}
+
+int cb_ipc_open(const void* handle, int device, void** ptr_out) {
+  if (handle == nullptr || ptr_out == nullptr) return fail(CB_ERR_INVALID, "null pointer");
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, 64);
+  cudaError_t e = cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return CB_OK;
+}
+
+int cb_ipc_close(void* ptr) {
+  if (ptr == nullptr) return CB_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return CB_OK;
+}
+
+int cb_enable_peer_access(int device, int peer) {
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+  if (!can) return fail(CB_ERR_UNSUPPORTED, "peer access not possible between these devices");
+  e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return CB_OK;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+  return CB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,266 @@
+// Bandwidth kernels of the handoff path and the generic CUDA-core mapper.
+//
+//  - rope_table_kernel      qwen_rope tables (src/cachebridge/rope.py:16-72)
+//  - derotate_pack_kernel   gather source key rows through the slot table,
+//                           remove source RoPE in FP32 (rope.py:82-89) and
+//                           store BF16 content-space keys for the tensor-core
+//                           mapper (the key half of pack_source_block,
+//                           online/blocks.py:47-82, fused with mapper.py:143-144)
+//  - copy_rows_kernel       row gather / scatter between row sets (pack_source_block
+//                           and _DirectMappedPoolCodec.copy)
+//  - map_install_simt_kernel  the full headwise mapper for geometries outside
+//                           the tensor-core path (head_dim != 128 or FP32 storage)
+#include "cb_device.cuh"
+#include "cb_kernels.cuh"
+
+namespace cbk {
+
+// ---------------------------------------------------------------------------
+// RoPE tables
+// ---------------------------------------------------------------------------
+__global__ void rope_table_kernel(const __grid_constant__ RopeTableParams p) {
+  const int64_t total = p.n * p.half_dim;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = idx / p.half_dim;
+    const int i = static_cast<int>(idx - t * p.half_dim);
+    const float pos = static_cast<float>(p.position_start + t);
+    const float phase = __fmul_rn(pos, p.inv_freq[i]);
+    float sn, cs;
+    sincosf(phase, &sn, &cs);
+    p.out_cos[idx] = __fmul_rn(cs, p.magnitude);
+    p.out_sin[idx] = __fmul_rn(sn, p.magnitude);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Key gather + source-RoPE removal -> BF16 content-space workspace
+// ---------------------------------------------------------------------------
+// One warp per token. Lane = (row group g = lane/8, pair index j = lane%8):
+// it owns elements [8j, 8j+8) and [64+8j, 64+8j+8) of one 128-wide head row,
+// i.e. 8 complete RoPE pairs, so the rotation needs no data exchange. Four
+// consecutive heads of the same slot row are read per warp instruction (1 KB
+// contiguous per instruction pair).
+__global__ void __launch_bounds__(256) derotate_pack_kernel(const __grid_constant__ DerotateParams p) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  if (t >= p.n_tokens) return;
+  const int g = lane >> 3;
+  const int j = lane & 7;
+
+  int64_t slot = load_slot(p.src_slots, p.src_slot_dtype, t);
+  if (slot < 0 || slot >= p.src_rows) {
+    if (lane == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+    slot = -1;
+  }
+  float c[8], s[8];
+  {
+    const float4* cp = reinterpret_cast<const float4*>(p.scos + t * 64 + 8 * j);
+    const float4* sp = reinterpret_cast<const float4*>(p.ssin + t * 64 + 8 * j);
+    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+    s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
+  }
+  const int rows = p.U * p.H;
+  const int64_t src_off = slot * p.src_row_stride;
+  constexpr int kUnroll = 4;
+  for (int r0 = 0; r0 < rows; r0 += 4 * kUnroll) {
+    uint4 a[kUnroll], b[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int r = r0 + 4 * k + g;
+      a[k] = make_uint4(0, 0, 0, 0);
+      b[k] = make_uint4(0, 0, 0, 0);
+      if (r < rows && slot >= 0) {
+        const int u = r / p.H;
+        const int h = r - u * p.H;
+        const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(p.src_k[__ldg(p.used + u)]) +
+                                   src_off + static_cast<int64_t>(p.src_head_offset + h) * 128;
+        a[k] = __ldg(reinterpret_cast<const uint4*>(row + 8 * j));
+        b[k] = __ldg(reinterpret_cast<const uint4*>(row + 64 + 8 * j));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int r = r0 + 4 * k + g;
+      if (r >= rows) continue;
+      const int u = r / p.H;
+      const int h = r - u * p.H;
+      const uint32_t av[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+      const uint32_t bv[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
+      uint32_t oa[4], ob[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x0l = bf16_lo(av[e]), x0h = bf16_hi(av[e]);
+        float x1l = bf16_lo(bv[e]), x1h = bf16_hi(bv[e]);
+        float y0l, y1l, y0h, y1h;
+        rope_remove_pair(x0l, x1l, c[2 * e], s[2 * e], y0l, y1l);
+        rope_remove_pair(x0h, x1h, c[2 * e + 1], s[2 * e + 1], y0h, y1h);
+        oa[e] = pack_bf16x2(y0l, y0h);
+        ob[e] = pack_bf16x2(y1l, y1h);
+      }
+      __nv_bfloat16* out = p.ws + ((static_cast<int64_t>(u) * p.n_tokens + t) * p.H + h) * 128;
+      *reinterpret_cast<uint4*>(out + 8 * j) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+      *reinterpret_cast<uint4*>(out + 64 + 8 * j) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row copies (gather / scatter)
+// ---------------------------------------------------------------------------
+// One warp per (kind, layer, token) row; VEC-byte vectors across lanes.
+template <typename V>
+__global__ void __launch_bounds__(256) copy_rows_kernel(const __grid_constant__ CopyRowsParams p) {
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t rows_total = 2 * static_cast<int64_t>(p.layers) * p.n;
+  const int lane = threadIdx.x & 31;
+  const int nvec = p.row_bytes / static_cast<int>(sizeof(V));
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       w < rows_total; w += warps_total) {
+    const int64_t t = w % p.n;
+    const int64_t kl = w / p.n;
+    const int layer = static_cast<int>(kl % p.layers);
+    const int kind = static_cast<int>(kl / p.layers);
+    const int64_t ss = load_slot(p.src_slots, p.src_slot_dtype, t);
+    const int64_t ds = load_slot(p.dst_slots, p.dst_slot_dtype, t);
+    if (ss < 0 || ss >= p.src_rows || ds < 0 || ds >= p.dst_rows) {
+      if (lane == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+      continue;
+    }
+    const char* src = reinterpret_cast<const char*>(kind ? p.src_v[layer] : p.src_k[layer]) +
+                      ss * p.src_stride_bytes + p.src_offset_bytes;
+    char* dst = reinterpret_cast<char*>(kind ? p.dst_v[layer] : p.dst_k[layer]) +
+                ds * p.dst_stride_bytes + p.dst_offset_bytes;
+    for (int e = lane; e < nvec; e += 32) {
+      reinterpret_cast<V*>(dst)[e] = reinterpret_cast<const V*>(src)[e];
+    }
+  }
+}
+
+cudaError_t launch_copy_rows(int vec_bytes, const CopyRowsParams& p, int blocks, cudaStream_t st) {
+  switch (vec_bytes) {
+    case 16: copy_rows_kernel<uint4><<<blocks, 256, 0, st>>>(p); break;
+    case 8: copy_rows_kernel<uint2><<<blocks, 256, 0, st>>>(p); break;
+    case 4: copy_rows_kernel<uint32_t><<<blocks, 256, 0, st>>>(p); break;
+    default: copy_rows_kernel<uint16_t><<<blocks, 256, 0, st>>>(p); break;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Generic (CUDA-core) headwise mapper
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// grid (n_tokens, L_t, 2 kinds). Shared memory: X [H][S*D] then Y [H][D] floats.
+template <typename T>
+__global__ void __launch_bounds__(256) map_install_simt_kernel(const __grid_constant__ SimtParams p) {
+  extern __shared__ float sm_f[];
+  const int64_t t = blockIdx.x;
+  const int l = blockIdx.y;
+  const int kind = blockIdx.z;
+  const int D = p.D;
+  const int half = D / 2;
+  const int F = p.S * D;
+  float* X = sm_f;
+  float* Y = sm_f + p.H * F;
+
+  const int64_t ss = load_slot(p.src_slots, p.src_slot_dtype, t);
+  const int64_t ds = load_slot(p.dst_slots, p.dst_slot_dtype, t);
+  if (ss < 0 || ss >= p.src_rows || ds < 0 || ds >= p.dst_rows) {
+    if (threadIdx.x == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+    return;
+  }
+  for (int idx = threadIdx.x; idx < p.H * F; idx += blockDim.x) {
+    const int h = idx / F;
+    const int f = idx - h * F;
+    const int j = f / D;
+    const int e = f - j * D;
+    const int layer = __ldg(p.sel + l * p.S + j);
+    const T* row = reinterpret_cast<const T*>(kind ? p.src_v[layer] : p.src_k[layer]) +
+                   ss * p.src_row_stride + static_cast<int64_t>(p.src_head_offset + h) * D;
+    float x = to_f32<T>(row[e]);
+    if (kind == 0) {
+      const int i = e < half ? e : e - half;
+      const float c = __ldg(p.scos + t * half + i);
+      const float s = __ldg(p.ssin + t * half + i);
+      float o0, o1;
+      if (e < half) {
+        rope_remove_pair(x, to_f32<T>(row[e + half]), c, s, o0, o1);
+        x = o0;
+      } else {
+        rope_remove_pair(to_f32<T>(row[e - half]), x, c, s, o0, o1);
+        x = o1;
+      }
+    }
+    X[idx] = x;
+  }
+  __syncthreads();
+  const float* W = p.w32 + ((static_cast<int64_t>(kind) * p.L_t + l) * p.H) * F * D;
+  const float* B = p.b32 + ((static_cast<int64_t>(kind) * p.L_t + l) * p.H) * D;
+  for (int idx = threadIdx.x; idx < p.H * D; idx += blockDim.x) {
+    const int h = idx / D;
+    const int d = idx - h * D;
+    const float* wh = W + static_cast<int64_t>(h) * F * D + d;
+    const float* xh = X + h * F;
+    float acc = 0.f;
+    for (int f = 0; f < F; ++f) acc = fmaf(xh[f], __ldg(wh + static_cast<int64_t>(f) * D), acc);
+    Y[idx] = __fadd_rn(acc, __ldg(B + idx));
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < p.H * D; idx += blockDim.x) {
+    const int h = idx / D;
+    const int d = idx - h * D;
+    float y = Y[idx];
+    if (kind == 0) {
+      const int i = d < half ? d : d - half;
+      const float c = __ldg(p.dcos + t * half + i);
+      const float s = __ldg(p.dsin + t * half + i);
+      float o0, o1;
+      if (d < half) {
+        rope_apply_pair(y, Y[idx + half], c, s, o0, o1);
+        y = o0;
+      } else {
+        rope_apply_pair(Y[idx - half], y, c, s, o0, o1);
+        y = o1;
+      }
+    }
+    T* out = reinterpret_cast<T*>(kind ? p.dst_v[l] : p.dst_k[l]) + ds * p.dst_row_stride +
+             static_cast<int64_t>(p.dst_head_offset + h) * D;
+    out[d] = from_f32<T>(y);
+  }
+}
+
+cudaError_t launch_map_simt(bool fp32_storage, const SimtParams& p, dim3 grid, size_t smem, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  if (fp32_storage) {
+    if (smem > 48 * 1024)
+      e = cudaFuncSetAttribute(map_install_simt_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    map_install_simt_kernel<float><<<grid, 256, smem, st>>>(p);
+  } else {
+    if (smem > 48 * 1024)
+      e = cudaFuncSetAttribute(map_install_simt_kernel<__nv_bfloat16>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    map_install_simt_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace cbk

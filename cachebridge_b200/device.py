@@ -1,0 +1,243 @@
+"""Torch-facing wrappers of the C-ABI launches (rows, RoPE tables, status).
+
+Everything here runs on CUDA devices only and launches on the caller's current
+torch stream. Buffers handed to the kernels (RoPE tables, the key workspace,
+the device status word) come from torch's caching allocator; the C-ABI calls
+themselves never allocate.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native as nat
+from .rope import rope_parameters
+
+_DTYPES = {torch.bfloat16: nat.CB_DTYPE_BF16, torch.float32: nat.CB_DTYPE_F32}
+
+
+def storage_dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported KV storage dtype {dtype}; expected bfloat16 or float32") from None
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if t.device.type != "cuda":
+        raise ValueError(f"{what} must be a CUDA tensor (cachebridge_b200 runs on GPUs only)")
+
+
+def slot_code(slots: torch.Tensor | None) -> int:
+    if slots is None:
+        return nat.CB_INDEX_NONE
+    if slots.dtype == torch.int32:
+        return nat.CB_INDEX_I32
+    if slots.dtype == torch.int64:
+        return nat.CB_INDEX_I64
+    raise ValueError("one-dimensional integer pool indices required")
+
+
+@dataclass
+class RowSet:
+    """Per-layer row buffers [rows, heads, head_dim] on one device.
+
+    The C-ABI view of an SGLang ``MHATokenToKVPool`` (``_get_key_buffer(l)`` /
+    ``_get_value_buffer(l)``) or of a dense page ``[2, layers, tokens, heads,
+    head_dim]`` (row = token).
+    """
+
+    k: list
+    v: list
+    heads: int
+    head_dim: int
+    head_offset: int = 0
+    slots: torch.Tensor | None = None
+    _keep: list = field(default_factory=list, repr=False)
+
+    @property
+    def layers(self) -> int:
+        return len(self.k)
+
+    @property
+    def device(self) -> torch.device:
+        return self.k[0].device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.k[0].dtype
+
+    @property
+    def rows(self) -> int:
+        return int(self.k[0].shape[0])
+
+    @staticmethod
+    def from_pool(pool, slots=None, head_offset: int = 0) -> "RowSet":
+        layers = range(pool.start_layer, pool.start_layer + pool.layer_num)
+        k = [pool._get_key_buffer(l) for l in layers]
+        v = [pool._get_value_buffer(l) for l in layers]
+        heads, dim = k[0].shape[1:]
+        return RowSet(k, v, int(heads), int(dim), head_offset, slots)
+
+    @staticmethod
+    def from_page(page: torch.Tensor, head_offset: int = 0) -> "RowSet":
+        if page.ndim != 5 or page.shape[0] != 2:
+            raise ValueError("source page must be [2,layers,tokens,kv_heads,head_dim]")
+        if not page.is_contiguous():
+            page = page.contiguous()
+        k = [page[0, l] for l in range(page.shape[1])]
+        v = [page[1, l] for l in range(page.shape[1])]
+        rs = RowSet(k, v, int(page.shape[3]), int(page.shape[4]), head_offset, None)
+        rs._keep.append(page)
+        return rs
+
+    def validate(self) -> int:
+        """Check layer geometry; return the common row stride (elements)."""
+        stride = None
+        for t in list(self.k) + list(self.v):
+            require_cuda(t, "KV rows")
+            if t.ndim != 3 or t.shape[1] != self.heads or t.shape[2] != self.head_dim:
+                raise ValueError("pool layers must be [rows, heads, head_dim]")
+            if t.stride(2) != 1 or t.stride(1) != self.head_dim:
+                raise ValueError("pool rows must be contiguous [heads, head_dim]")
+            if t.dtype != self.dtype or t.device != self.device or t.shape[0] != self.rows:
+                raise ValueError("pool layers must share dtype, device and row count")
+            if stride is None:
+                stride = t.stride(0)
+            elif t.stride(0) != stride:
+                raise ValueError("pool layers must share one row stride")
+        if self.slots is not None:
+            require_cuda(self.slots, "slot indices")
+            if self.slots.ndim != 1:
+                raise ValueError("one-dimensional integer pool indices required")
+            if self.slots.device != self.device:
+                raise ValueError("pool, indices and workspace must share device and dtype as applicable")
+            if not self.slots.is_contiguous():
+                self.slots = self.slots.contiguous()
+        return int(stride)
+
+    def to_c(self) -> nat.CbRows:
+        stride = self.validate()
+        karr = nat.pointer_array([t.data_ptr() for t in self.k])
+        varr = nat.pointer_array([t.data_ptr() for t in self.v])
+        self._keep.extend([karr, varr])
+        return nat.CbRows(
+            layers=self.layers,
+            heads=self.heads,
+            k=ctypes.cast(karr, ctypes.POINTER(ctypes.c_void_p)),
+            v=ctypes.cast(varr, ctypes.POINTER(ctypes.c_void_p)),
+            row_stride=stride,
+            rows=self.rows,
+            head_offset=self.head_offset,
+            slot_dtype=slot_code(self.slots),
+            slots=None if self.slots is None else self.slots.data_ptr(),
+        )
+
+
+def current_stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_status_words: dict = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word the kernels OR their CB_DEV_ERR_* bits into."""
+    key = torch.device(device).index
+    word = _status_words.get(key)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _status_words[key] = word
+    return word
+
+
+def read_status(device: torch.device, clear: bool = True) -> int:
+    """Synchronize the current stream and return (then clear) the status bits."""
+    word = status_word(device)
+    value = int(word.item())
+    if clear and value:
+        word.zero_()
+    return value
+
+
+def raise_for_status(device: torch.device) -> None:
+    bits = read_status(device)
+    if bits & nat.CB_DEV_ERR_SLOT_RANGE:
+        raise ValueError("a pool slot index was outside the pool (device check)")
+    if bits & nat.CB_DEV_ERR_TIMEOUT:
+        raise RuntimeError("a bounded pipeline wait expired inside a handoff kernel")
+    if bits:
+        raise RuntimeError(f"handoff kernel reported device status {bits}")
+
+
+def rope_tables(
+    device: torch.device,
+    head_dim: int,
+    theta: float,
+    scaling: dict | None,
+    position_start: int,
+    n: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin tables [n, head_dim/2] (FP32) for positions position_start..+n-1."""
+    lib = nat.load()
+    inv_freq, magnitude = rope_parameters(head_dim, theta, scaling)
+    half = head_dim // 2
+    cos = torch.empty((max(n, 1), half), dtype=torch.float32, device=device)
+    sin = torch.empty_like(cos)
+    arr = (ctypes.c_float * half)(*inv_freq.tolist())
+    nat.check(
+        lib.cb_rope_table(
+            ctypes.c_void_p(current_stream_ptr(device)),
+            arr,
+            half,
+            ctypes.c_float(magnitude),
+            int(position_start),
+            int(n),
+            cos.data_ptr(),
+            sin.data_ptr(),
+        ),
+        "cb_rope_table",
+    )
+    return cos, sin
+
+
+def pack_rows(src: RowSet, n: int, out: torch.Tensor) -> torch.Tensor:
+    """Gather rows ``src.slots[:n]`` of every layer into dense ``out``."""
+    lib = nat.load()
+    status = status_word(src.device)
+    c = src.to_c()
+    nat.check(
+        lib.cb_pack_rows(
+            ctypes.c_void_p(current_stream_ptr(src.device)),
+            ctypes.byref(c),
+            src.head_dim,
+            storage_dtype_code(src.dtype),
+            int(n),
+            out.data_ptr(),
+            status.data_ptr(),
+        ),
+        "cb_pack_rows",
+    )
+    return out
+
+
+def install_rows(block: torch.Tensor, dst: RowSet, n: int) -> None:
+    """Scatter dense ``block`` [2, layers, n, heads, dim] into rows ``dst.slots``."""
+    lib = nat.load()
+    status = status_word(dst.device)
+    c = dst.to_c()
+    nat.check(
+        lib.cb_install_rows(
+            ctypes.c_void_p(current_stream_ptr(dst.device)),
+            block.data_ptr(),
+            ctypes.byref(c),
+            dst.head_dim,
+            storage_dtype_code(dst.dtype),
+            int(n),
+            status.data_ptr(),
+        ),
+        "cb_install_rows",
+    )

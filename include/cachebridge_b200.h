@@ -1,0 +1,216 @@
+/*
+ * cachebridge_b200 — C ABI of the B200 (sm_100a) CacheBridge handoff hot path.
+ *
+ * The reference implements this path in PyTorch (src/cachebridge/mapper.py,
+ * src/cachebridge/online/blocks.py and the SGLang runtime adapters). Every
+ * entry point below replaces one reference interface; the comment above each
+ * declaration names the reference file:line it stands in for.
+ *
+ * Conventions
+ *  - All pointers to tensor data are DEVICE pointers owned by the caller,
+ *    except where a parameter is documented as a host array.
+ *  - Calls that launch work are asynchronous on the caller's CUDA stream
+ *    (`stream` is a cudaStream_t passed as void*; NULL = legacy default stream).
+ *  - Return value: CB_OK (0) or a negative CB_ERR_* code. No call throws across
+ *    the ABI. cb_last_error() returns a thread-local message for the last
+ *    failure on the calling thread.
+ *  - Hot-path calls (cb_map_install, cb_pack_rows, cb_install_rows,
+ *    cb_rope_table) never allocate device or host memory. cb_mapper_create is
+ *    the only allocating call besides the IPC helpers.
+ *  - Row indices (slots) are validated on the device: an index outside
+ *    [0, rows) is skipped and CB_DEV_ERR_SLOT_RANGE is OR-ed into the caller's
+ *    device status word, which the caller reads after the stream completes.
+ *
+ * Data model
+ *  A "row set" (cb_rows) is a per-layer array of row-addressed buffers, which
+ *  is exactly an SGLang MHATokenToKVPool (k_buffer[l] / v_buffer[l] with rows
+ *  of [heads, head_dim]) or a dense page [2, layers, tokens, heads, head_dim]
+ *  seen as per-layer pointers with slot = token.
+ */
+#ifndef CACHEBRIDGE_B200_H
+#define CACHEBRIDGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CB_API __attribute__((visibility("default")))
+#else
+#define CB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host status codes. */
+#define CB_OK 0
+#define CB_ERR_INVALID -1     /* bad geometry, pointer alignment or argument */
+#define CB_ERR_UNSUPPORTED -2 /* valid request outside what this build supports */
+#define CB_ERR_CUDA -3        /* a CUDA runtime call failed */
+#define CB_ERR_ALIAS -4       /* destination rows alias (install) */
+
+/* Device status bits, OR-ed into the caller's int32 status word. */
+#define CB_DEV_ERR_SLOT_RANGE 1 /* a source or destination slot was outside [0, rows) */
+#define CB_DEV_ERR_TIMEOUT 2    /* a bounded pipeline wait inside a kernel expired */
+
+/* Storage dtypes. */
+#define CB_DTYPE_F32 0
+#define CB_DTYPE_BF16 1
+
+/* Slot index dtypes (0 = no index array: row t of the set is row t). */
+#define CB_INDEX_NONE 0
+#define CB_INDEX_I32 32
+#define CB_INDEX_I64 64
+
+/* Maximum layers in one row set (kernel parameter arrays are sized by it). */
+#define CB_MAX_LAYERS 128
+
+typedef struct cb_rows {
+  int32_t layers;          /* number of per-layer buffers */
+  int32_t heads;           /* heads per row (row = heads * head_dim elements) */
+  void* const* k;          /* HOST array [layers] of device pointers to K rows */
+  void* const* v;          /* HOST array [layers] of device pointers to V rows */
+  int64_t row_stride;      /* elements between consecutive rows */
+  int64_t rows;            /* addressable rows per layer (bound for slots) */
+  int32_t head_offset;     /* head index inside a row of this call's head 0 */
+  int32_t slot_dtype;      /* CB_INDEX_* */
+  const void* slots;       /* device [n_tokens] row indices, or NULL */
+} cb_rows;
+
+typedef struct cb_mapper cb_mapper;
+
+/* Library version (major*10000 + minor*100 + patch). */
+CB_API int cb_version(void);
+/* Human-readable text for a host status code. */
+CB_API const char* cb_status_string(int status);
+/* Thread-local message describing the last failing call on this thread. */
+CB_API const char* cb_last_error(void);
+
+/*
+ * Upload one head-local (CacheBridge, "headwise") mapper for a target TP rank.
+ * Replaces PageMapper.__init__ (src/cachebridge/mapper.py:35-110): the caller
+ * has already loaded layer_NNN.safetensors and sliced its target heads
+ * (mapper.py:75-107); this call takes the sliced FP32 tensors (host memory):
+ *   selected [target_layers][num_selected] int64   (mapper.py:95)
+ *   k_weight, v_weight [target_layers][heads][num_selected*head_dim][head_dim]
+ *   k_bias,   v_bias   [target_layers][heads][head_dim]
+ * Weights are kept on `device` in FP32 (generic kernel) and, for head_dim 128,
+ * also as a BF16 tensor-core image (rounded to nearest even).
+ */
+CB_API int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads,
+                     int head_dim, int num_selected, const int64_t* selected,
+                     const float* k_weight, const float* k_bias,
+                     const float* v_weight, const float* v_bias);
+/* Free a mapper and its device memory. */
+CB_API int cb_mapper_destroy(cb_mapper* mapper);
+/* Geometry of an uploaded mapper (any output pointer may be NULL). */
+CB_API int cb_mapper_info(const cb_mapper* mapper, int* target_layers, int* heads,
+                   int* head_dim, int* num_selected, int* used_source_layers);
+/*
+ * Bytes of caller-provided scratch that cb_map_install needs for n_tokens
+ * tokens of `dtype` storage (0 when the call needs none).
+ */
+CB_API size_t cb_mapper_workspace_bytes(const cb_mapper* mapper, int dtype,
+                                 int64_t n_tokens);
+
+/*
+ * Split-half (Qwen) RoPE tables for positions position_start .. +n-1:
+ *   cos[t][i] = cos(float(p_t) * inv_freq[i]) * magnitude, sin likewise,
+ * i < half_dim. inv_freq is a HOST array [half_dim] (at most 128 values).
+ * Replaces qwen_rope (src/cachebridge/rope.py:16-72), whose cat(phase, phase)
+ * duplicate half is implied. Outputs are device [n][half_dim] FP32.
+ */
+CB_API int cb_rope_table(void* stream, const float* inv_freq, int half_dim,
+                  float magnitude, int64_t position_start, int64_t n,
+                  float* out_cos, float* out_sin);
+
+/*
+ * Fused pack + mapper apply + install for n_tokens tokens.
+ * Replaces, in one call, pack_source_block (src/cachebridge/online/blocks.py:47-82),
+ * PageMapper.map_page headwise branch (src/cachebridge/mapper.py:116-181, 207-239;
+ * head narrowing src/cachebridge/online/mapping.py:7-33) and the install
+ * (blocks.py:86-111 map_write_block / set_kv_buffer, and
+ * backends/sglang/runtime/source_mapper_adapter.py:389-425 _DirectMappedPoolCodec.copy).
+ *   src: source rows, src->layers >= 1 + max(selected); token t reads row
+ *        src->slots[t]; target head h reads source head src->head_offset + h.
+ *   dst: target rows, dst->layers == target_layers; token t of target head h
+ *        is written to row dst->slots[t], head dst->head_offset + h. dst
+ *        pointers may be peer-device pointers (CUDA IPC / peer access).
+ *   src_cos/src_sin, dst_cos/dst_sin: cb_rope_table outputs for the tokens'
+ *        absolute positions (source and target RoPE).
+ *   dtype: storage dtype of src and dst rows (CB_DTYPE_BF16 or CB_DTYPE_F32).
+ *   workspace: >= cb_mapper_workspace_bytes(mapper, dtype, n_tokens) bytes.
+ *   dev_status: device int32 status word (CB_DEV_ERR_* bits are OR-ed in).
+ * Compute: keys have the source RoPE removed in FP32, features of the S
+ * selected source layers are concatenated, y = x W + b is accumulated in FP32,
+ * target RoPE is applied to keys in FP32, and the result is rounded to the
+ * storage dtype. BF16 rows with head_dim 128 run on tcgen05 tensor cores
+ * (BF16 operands, FP32 accumulation); other geometries on a CUDA-core kernel.
+ */
+CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
+                   const cb_rows* dst, int64_t n_tokens, const float* src_cos,
+                   const float* src_sin, const float* dst_cos,
+                   const float* dst_sin, int dtype, void* workspace,
+                   size_t workspace_bytes, int32_t* dev_status);
+
+/*
+ * The two phases of cb_map_install's tensor-core path as separate calls
+ * (head_dim 128, BF16 storage only), mirroring the reference's pack -> map
+ * split (online/blocks.py:47-82 then mapper.py:116-239):
+ *  cb_derotate_keys: gather the source key rows of every used source layer
+ *    through src->slots, remove the source RoPE in FP32 (rope.py:82-89,
+ *    mapper.py:143-144) and store BF16 content-space keys in `workspace`
+ *    ([used_layers][n_tokens][heads][128]).
+ *  cb_map_install_packed: map keys from `workspace` and values from the
+ *    source rows, apply bias and target RoPE, and install into dst rows.
+ * cb_map_install(...) == cb_derotate_keys(...) then cb_map_install_packed(...)
+ * on the same stream.
+ */
+CB_API int cb_derotate_keys(cb_mapper* mapper, void* stream, const cb_rows* src,
+                     int64_t n_tokens, const float* src_cos, const float* src_sin,
+                     void* workspace, size_t workspace_bytes, int32_t* dev_status);
+CB_API int cb_map_install_packed(cb_mapper* mapper, void* stream, const cb_rows* src,
+                          const cb_rows* dst, int64_t n_tokens, const float* dst_cos,
+                          const float* dst_sin, const void* workspace,
+                          size_t workspace_bytes, int32_t* dev_status);
+
+/*
+ * Row gather: out[kind][l][t][:] = src.{k,v}[l][src.slots[t]][row] for all
+ * src.layers layers, kinds K then V; `row` = src.heads*head_dim elements
+ * starting at head src.head_offset. out is a dense device buffer
+ * [2][layers][n_tokens][heads*head_dim].
+ * Replaces pack_source_block (src/cachebridge/online/blocks.py:47-82).
+ */
+CB_API int cb_pack_rows(void* stream, const cb_rows* src, int head_dim, int dtype,
+                 int64_t n_tokens, void* out, int32_t* dev_status);
+
+/*
+ * Row scatter: dst.{k,v}[l][dst.slots[t]][row] = block[kind][l][t][:].
+ * block is dense [2][layers][n_tokens][heads*head_dim] and may live on a peer
+ * device. Replaces _DirectMappedPoolCodec.copy
+ * (backends/sglang/runtime/source_mapper_adapter.py:389-425) and the
+ * cudaMemcpyPeerAsync span loop (backends/sglang/runtime/peer_adapter.py:211-282,
+ * peer_runtime.py:55-64) with one launch.
+ */
+CB_API int cb_install_rows(void* stream, const void* block, const cb_rows* dst,
+                    int head_dim, int dtype, int64_t n_tokens,
+                    int32_t* dev_status);
+
+/*
+ * CUDA IPC helpers for the tensor-parallel transfer: export a device
+ * allocation (64-byte handle) and map a peer's allocation into this process.
+ * They stand in for torch's reduce_tensor / rebuild_cuda_tensor used by
+ * backends/sglang/runtime/bounded_handoff_channel.py:83-123.
+ */
+CB_API int cb_ipc_export(const void* device_ptr, void* handle_out /* 64 bytes */);
+CB_API int cb_ipc_open(const void* handle /* 64 bytes */, int device, void** ptr_out);
+CB_API int cb_ipc_close(void* ptr);
+/* Enable direct peer access from `device` to `peer` (idempotent). */
+CB_API int cb_enable_peer_access(int device, int peer);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CACHEBRIDGE_B200_H */
