@@ -69,6 +69,16 @@ class CbRows(ctypes.Structure):
     ]
 
 
+class CbRope(ctypes.Structure):
+    """Mirror of ``struct cb_rope``."""
+
+    _fields_ = [
+        ("half_dim", ctypes.c_int32),
+        ("magnitude", ctypes.c_float),
+        ("inv_freq", ctypes.c_float * 128),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -90,6 +100,7 @@ def _declare(lib: ctypes.CDLL) -> None:
         ctypes.c_size_t,
     )
     rows_p = ctypes.POINTER(CbRows)
+    rope_p = ctypes.POINTER(CbRope)
     lib.cb_version.restype = c_int
     lib.cb_status_string.restype = ctypes.c_char_p
     lib.cb_status_string.argtypes = [c_int]
@@ -105,15 +116,15 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_mapper_workspace_bytes.restype = c_size
     lib.cb_mapper_workspace_bytes.argtypes = [c_vp, c_int, c_i64]
     lib.cb_rope_table.restype = c_int
-    lib.cb_rope_table.argtypes = [c_vp, c_vp, c_int, c_float, c_i64, c_i64, c_vp, c_vp]
+    lib.cb_rope_table.argtypes = [c_vp, rope_p, c_i64, c_i64, c_vp, c_vp, c_i64]
     lib.cb_map_install.restype = c_int
     lib.cb_map_install.argtypes = [
-        c_vp, c_vp, rows_p, rows_p, c_i64, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_size, c_vp
+        c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp, c_size, c_vp
     ]
     lib.cb_derotate_keys.restype = c_int
-    lib.cb_derotate_keys.argtypes = [c_vp, c_vp, rows_p, c_i64, c_vp, c_vp, c_vp, c_size, c_vp]
+    lib.cb_derotate_keys.argtypes = [c_vp, c_vp, rows_p, c_i64, c_i64, rope_p, rope_p, c_vp, c_size, c_vp]
     lib.cb_map_install_packed.restype = c_int
-    lib.cb_map_install_packed.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_vp, c_vp, c_vp, c_size, c_vp]
+    lib.cb_map_install_packed.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_vp, c_size, c_vp]
     lib.cb_pack_rows.restype = c_int
     lib.cb_pack_rows.argtypes = [c_vp, rows_p, c_int, c_int, c_i64, c_vp, c_vp]
     lib.cb_install_rows.restype = c_int

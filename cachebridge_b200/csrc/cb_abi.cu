@@ -86,6 +86,22 @@ int check_rows(const cb_rows* r, const char* name, int head_dim, int heads_used,
 
 std::once_flag g_tc_attr_once[64];
 
+int check_rope(const cb_rope* r, int head_dim, const char* name) {
+  if (r == nullptr) return fail(CB_ERR_INVALID, std::string(name) + ": null RoPE descriptor");
+  if (r->half_dim * 2 != head_dim || r->half_dim > 128)
+    return fail(CB_ERR_INVALID, std::string(name) + ": RoPE half_dim does not match head_dim");
+  if (!std::isfinite(r->magnitude)) return fail(CB_ERR_INVALID, std::string(name) + ": non-finite RoPE magnitude");
+  return CB_OK;
+}
+
+cbk::RopeDev rope_dev(const cb_rope* r) {
+  cbk::RopeDev d{};
+  std::memcpy(d.inv_freq, r->inv_freq, sizeof(float) * r->half_dim);
+  d.magnitude = r->magnitude;
+  d.half_dim = r->half_dim;
+  return d;
+}
+
 }  // namespace
 
 struct cb_mapper {
@@ -105,10 +121,22 @@ struct cb_mapper {
 namespace {
 
 int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
-                    size_t workspace_bytes, const float* cos, const float* sin);
+                    size_t workspace_bytes);
+
+// Tensor-core workspace: BF16 content-space keys [U][n][H][128], then the
+// target RoPE coefficient tables cos [64][n] and sin [64][n] (FP32), 256-byte aligned.
+size_t ws_keys_bytes(const cb_mapper* m, int64_t n) {
+  return (static_cast<size_t>(m->U) * static_cast<size_t>(n) * m->H * cbk::kD * 2 + 255) & ~size_t(255);
+}
+size_t ws_table_bytes(int64_t n) { return (static_cast<size_t>(n) * 64 * 4 + 255) & ~size_t(255); }
+size_t ws_total_bytes(const cb_mapper* m, int64_t n) { return ws_keys_bytes(m, n) + 2 * ws_table_bytes(n); }
+
+int launch_rope_table(cudaStream_t st, const cb_rope* rope, int64_t position_start, int64_t n, float* out_cos,
+                      float* out_sin, int64_t out_stride);
 
 int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int64_t n_tokens,
-                    const float* src_cos, const float* src_sin, void* workspace, int32_t* dev_status) {
+                    int64_t position_start, const cb_rope* src_rope, const cb_rope* dst_rope, void* workspace,
+                    int32_t* dev_status) {
   cbk::DerotateParams dp{};
   dp.n_tokens = n_tokens;
   dp.H = m->H;
@@ -120,20 +148,21 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
   dp.src_head_offset = src->head_offset;
   dp.src_slot_dtype = src->slot_dtype;
   dp.src_slots = src->slots;
-  dp.scos = src_cos;
-  dp.ssin = src_sin;
+  dp.rope = rope_dev(src_rope);
+  dp.position_start = position_start;
   dp.ws = static_cast<__nv_bfloat16*>(workspace);
   dp.status = dev_status;
   const int blocks = static_cast<int>((n_tokens + 7) / 8);
   cbk::derotate_pack_kernel<<<blocks, 256, 0, st>>>(dp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "derotate_pack launch");
-  return CB_OK;
+  char* tables = static_cast<char*>(workspace) + ws_keys_bytes(m, n_tokens);
+  return launch_rope_table(st, dst_rope, position_start, n_tokens, reinterpret_cast<float*>(tables),
+                           reinterpret_cast<float*>(tables + ws_table_bytes(n_tokens)), n_tokens);
 }
 
 int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst,
-              int64_t n_tokens, const float* dst_cos, const float* dst_sin, const void* workspace,
-              int32_t* dev_status) {
+              int64_t n_tokens, const void* workspace, int32_t* dev_status) {
   cbk::MapTcParams p{};
   p.n_tokens = static_cast<int>(n_tokens);
   p.L_t = m->L_t;
@@ -169,8 +198,9 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.dst_head_offset = dst->head_offset;
   p.dst_slot_dtype = dst->slot_dtype;
   p.dst_slots = dst->slots;
-  p.dcos = dst_cos;
-  p.dsin = dst_sin;
+  const char* tables = static_cast<const char*>(workspace) + ws_keys_bytes(m, n_tokens);
+  p.dcos = reinterpret_cast<const float*>(tables);
+  p.dsin = reinterpret_cast<const float*>(tables + ws_table_bytes(n_tokens));
   p.status = dev_status;
   const int smem = cbk::tc_smem_bytes(p.w_slots, p.stages);
   cudaError_t attr_err = cudaSuccess;
@@ -187,14 +217,12 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
 }
 
 int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
-                    size_t workspace_bytes, const float* cos, const float* sin) {
-  const size_t need = static_cast<size_t>(m->U) * static_cast<size_t>(n_tokens) * m->H * cbk::kD * 2;
+                    size_t workspace_bytes) {
+  const size_t need = ws_total_bytes(m, n_tokens);
   if (m->D != cbk::kD || dtype != CB_DTYPE_BF16)
     return fail(CB_ERR_UNSUPPORTED, "tensor-core path needs head_dim 128 and bf16 storage");
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return fail(CB_ERR_INVALID, "workspace missing, too small or misaligned");
-  if (cos == nullptr || sin == nullptr) return fail(CB_ERR_INVALID, "null RoPE table");
-  if (!aligned16(cos) || !aligned16(sin)) return fail(CB_ERR_INVALID, "RoPE tables must be 16-byte aligned");
   return CB_OK;
 }
 
@@ -210,6 +238,23 @@ int check_tc_call(const cb_mapper* m, const cb_rows* src, const cb_rows* dst, in
     if ((rc = check_rows(dst, "dst", m->D, m->H, CB_DTYPE_BF16, true)) != CB_OK) return rc;
     if (dst->layers != m->L_t) return fail(CB_ERR_INVALID, "destination layer count != mapper target layers");
   }
+  return CB_OK;
+}
+
+int launch_rope_table(cudaStream_t st, const cb_rope* rope, int64_t position_start, int64_t n, float* out_cos,
+                      float* out_sin, int64_t out_stride) {
+  cbk::RopeTableParams p{};
+  p.rope = rope_dev(rope);
+  p.position_start = position_start;
+  p.n = n;
+  p.out_cos = out_cos;
+  p.out_sin = out_sin;
+  p.out_stride = out_stride;
+  const int64_t total = n * rope->half_dim;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  cbk::rope_table_kernel<<<blocks, 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope_table launch");
   return CB_OK;
 }
 
@@ -361,35 +406,24 @@ int cb_mapper_info(const cb_mapper* m, int* target_layers, int* heads, int* head
 size_t cb_mapper_workspace_bytes(const cb_mapper* m, int dtype, int64_t n_tokens) {
   if (m == nullptr || n_tokens <= 0) return 0;
   if (m->D != cbk::kD || dtype != CB_DTYPE_BF16) return 0;
-  return static_cast<size_t>(m->U) * static_cast<size_t>(n_tokens) * m->H * cbk::kD * 2;
+  return ws_total_bytes(m, n_tokens);
 }
 
-int cb_rope_table(void* stream, const float* inv_freq, int half_dim, float magnitude,
-                  int64_t position_start, int64_t n, float* out_cos, float* out_sin) {
-  if (inv_freq == nullptr || half_dim <= 0 || half_dim > 128 || n < 0 || position_start < 0)
+int cb_rope_table(void* stream, const cb_rope* rope, int64_t position_start, int64_t n, float* out_cos,
+                  float* out_sin, int64_t out_stride) {
+  if (rope == nullptr || rope->half_dim <= 0 || rope->half_dim > 128 || n < 0 || position_start < 0)
     return fail(CB_ERR_INVALID, "rope table: bad arguments");
   if (n == 0) return CB_OK;
   if (out_cos == nullptr || out_sin == nullptr) return fail(CB_ERR_INVALID, "rope table: null output");
-  cbk::RopeTableParams p{};
-  std::memcpy(p.inv_freq, inv_freq, sizeof(float) * half_dim);
-  p.half_dim = half_dim;
-  p.magnitude = magnitude;
-  p.position_start = position_start;
-  p.n = n;
-  p.out_cos = out_cos;
-  p.out_sin = out_sin;
-  const int64_t total = n * half_dim;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 65535));
-  cbk::rope_table_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "rope_table launch");
-  return CB_OK;
+  if (out_stride < n) return fail(CB_ERR_INVALID, "rope table: stride smaller than n");
+  return launch_rope_table(static_cast<cudaStream_t>(stream), rope, position_start, n, out_cos, out_sin,
+                           out_stride);
 }
 
 int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
-                   int64_t n_tokens, const float* src_cos, const float* src_sin,
-                   const float* dst_cos, const float* dst_sin, int dtype, void* workspace,
-                   size_t workspace_bytes, int32_t* dev_status) {
+                   int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
+                   const cb_rope* dst_rope, int dtype, void* workspace, size_t workspace_bytes,
+                   int32_t* dev_status) {
   if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
   if (dtype != CB_DTYPE_BF16 && dtype != CB_DTYPE_F32) return fail(CB_ERR_UNSUPPORTED, "dtype must be bf16 or fp32");
   if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
@@ -401,16 +435,19 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
   if (src->layers <= m->max_sel) return fail(CB_ERR_INVALID, "mapper selected layer exceeds source page depth");
   if (dst->layers != m->L_t) return fail(CB_ERR_INVALID, "destination layer count != mapper target layers");
   if (n_tokens == 0) return CB_OK;
-  if (!src_cos || !src_sin || !dst_cos || !dst_sin) return fail(CB_ERR_INVALID, "null RoPE table");
+  if ((rc = check_rope(src_rope, m->D, "source RoPE")) != CB_OK) return rc;
+  if ((rc = check_rope(dst_rope, m->D, "target RoPE")) != CB_OK) return rc;
+  if (position_start < 0) return fail(CB_ERR_INVALID, "negative position_start");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
 
   if (tc) {
-    if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes, src_cos, src_sin)) != CB_OK) return rc;
-    if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes, dst_cos, dst_sin)) != CB_OK) return rc;
-    if ((rc = launch_derotate(m, st, src, n_tokens, src_cos, src_sin, workspace, dev_status)) != CB_OK) return rc;
-    return launch_tc(m, st, src, dst, n_tokens, dst_cos, dst_sin, workspace, dev_status);
+    if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
+    if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, dst_rope, workspace, dev_status)) !=
+        CB_OK)
+      return rc;
+    return launch_tc(m, st, src, dst, n_tokens, workspace, dev_status);
   }
 
   // Generic CUDA-core path.
@@ -440,10 +477,9 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
   p.dst_head_offset = dst->head_offset;
   p.dst_slot_dtype = dst->slot_dtype;
   p.dst_slots = dst->slots;
-  p.scos = src_cos;
-  p.ssin = src_sin;
-  p.dcos = dst_cos;
-  p.dsin = dst_sin;
+  p.src_rope = rope_dev(src_rope);
+  p.dst_rope = rope_dev(dst_rope);
+  p.position_start = position_start;
   p.status = dev_status;
   const size_t smem = static_cast<size_t>(m->H) * (m->S * m->D + m->D) * sizeof(float);
   if (smem > static_cast<size_t>(cbk::kTcMaxSmem)) return fail(CB_ERR_UNSUPPORTED, "generic mapper: heads*features too large");
@@ -455,31 +491,31 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
 }
 
 int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_tokens,
-                     const float* src_cos, const float* src_sin, void* workspace,
-                     size_t workspace_bytes, int32_t* dev_status) {
+                     int64_t position_start, const cb_rope* src_rope, const cb_rope* dst_rope,
+                     void* workspace, size_t workspace_bytes, int32_t* dev_status) {
   int rc = check_tc_call(m, src, nullptr, n_tokens);
   if (rc != CB_OK) return rc;
+  if ((rc = check_rope(src_rope, m->D, "source RoPE")) != CB_OK) return rc;
+  if ((rc = check_rope(dst_rope, m->D, "target RoPE")) != CB_OK) return rc;
+  if (position_start < 0) return fail(CB_ERR_INVALID, "negative position_start");
   if (n_tokens == 0) return CB_OK;
-  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes, src_cos, src_sin)) != CB_OK)
-    return rc;
+  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
-  return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, src_cos, src_sin, workspace,
-                         dev_status);
+  return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, position_start, src_rope, dst_rope,
+                         workspace, dev_status);
 }
 
 int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
-                          int64_t n_tokens, const float* dst_cos, const float* dst_sin,
-                          const void* workspace, size_t workspace_bytes, int32_t* dev_status) {
+                          int64_t n_tokens, const void* workspace, size_t workspace_bytes,
+                          int32_t* dev_status) {
   int rc = check_tc_call(m, src, dst, n_tokens);
   if (rc != CB_OK) return rc;
   if (n_tokens == 0) return CB_OK;
-  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes, dst_cos, dst_sin)) != CB_OK)
-    return rc;
+  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
-  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, dst_cos, dst_sin, workspace,
-                   dev_status);
+  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, workspace, dev_status);
 }
 
 static int launch_copy_rows(cudaStream_t st, cbk::CopyRowsParams& p, int64_t n) {

@@ -28,6 +28,24 @@ struct RowSet {
   const void* slots;
 };
 
+// Device image of cb_rope.
+struct RopeDev {
+  float inv_freq[128];
+  float magnitude;
+  int half_dim;
+};
+
+// qwen_rope coefficients of one (position, frequency): the FP32 phase
+// float(position) * inv_freq, then cos/sin (CUDA's accurate sincosf) times the
+// YaRN magnitude, in the reference's op order (rope.py:70-72).
+__device__ __forceinline__ void rope_coeff(float pos, float inv_freq, float magnitude, float& c,
+                                           float& s) {
+  float sn, cs;
+  sincosf(__fmul_rn(pos, inv_freq), &sn, &cs);
+  c = __fmul_rn(cs, magnitude);
+  s = __fmul_rn(sn, magnitude);
+}
+
 __device__ __forceinline__ int64_t load_slot(const void* slots, int dtype, int64_t t) {
   if (dtype == CB_INDEX_I32) return (int64_t)__ldg(reinterpret_cast<const int32_t*>(slots) + t);
   if (dtype == CB_INDEX_I64) return (int64_t)__ldg(reinterpret_cast<const long long*>(slots) + t);
@@ -130,6 +148,16 @@ __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// Arrive on `bar` (without raising its pending count) once every cp.async this
+// thread issued so far has completed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -223,6 +251,17 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
 

@@ -19,17 +19,18 @@ namespace cbk {
 // RoPE tables
 // ---------------------------------------------------------------------------
 __global__ void rope_table_kernel(const __grid_constant__ RopeTableParams p) {
-  const int64_t total = p.n * p.half_dim;
+  const int half = p.rope.half_dim;
+  const int64_t total = p.n * half;
+  // Token-fastest order: consecutive threads write consecutive columns of one
+  // frequency row (coalesced stores into the frequency-major table).
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = idx / p.half_dim;
-    const int i = static_cast<int>(idx - t * p.half_dim);
-    const float pos = static_cast<float>(p.position_start + t);
-    const float phase = __fmul_rn(pos, p.inv_freq[i]);
-    float sn, cs;
-    sincosf(phase, &sn, &cs);
-    p.out_cos[idx] = __fmul_rn(cs, p.magnitude);
-    p.out_sin[idx] = __fmul_rn(sn, p.magnitude);
+    const int i = static_cast<int>(idx / p.n);
+    const int64_t t = idx - static_cast<int64_t>(i) * p.n;
+    float c, s;
+    rope_coeff(static_cast<float>(p.position_start + t), p.rope.inv_freq[i], p.rope.magnitude, c, s);
+    p.out_cos[i * p.out_stride + t] = c;
+    p.out_sin[i * p.out_stride + t] = s;
   }
 }
 
@@ -41,7 +42,13 @@ __global__ void rope_table_kernel(const __grid_constant__ RopeTableParams p) {
 // i.e. 8 complete RoPE pairs, so the rotation needs no data exchange. Four
 // consecutive heads of the same slot row are read per warp instruction (1 KB
 // contiguous per instruction pair).
-__global__ void __launch_bounds__(256) derotate_pack_kernel(const __grid_constant__ DerotateParams p) {
+//
+// The reference divides by max(cos^2 + sin^2, FLT_MIN) per element
+// (rope.py:86-89). The result here is rounded to BF16 (the tensor-core operand),
+// so the division is folded once per (token, frequency) into the coefficients
+// cos/m and sin/m; the two forms differ by at most a few FP32 ulps before the
+// BF16 rounding.
+__global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_constant__ DerotateParams p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + warp;
@@ -56,11 +63,16 @@ __global__ void __launch_bounds__(256) derotate_pack_kernel(const __grid_constan
   }
   float c[8], s[8];
   {
-    const float4* cp = reinterpret_cast<const float4*>(p.scos + t * 64 + 8 * j);
-    const float4* sp = reinterpret_cast<const float4*>(p.ssin + t * 64 + 8 * j);
-    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-    s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
+    const float pos = static_cast<float>(p.position_start + t);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) rope_coeff(pos, p.rope.inv_freq[8 * j + e], p.rope.magnitude, c[e], s[e]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float m = fmaxf(__fadd_rn(__fmul_rn(c[e], c[e]), __fmul_rn(s[e], s[e])), 1.17549435e-38f);
+      const float inv = __frcp_rn(m);
+      c[e] = __fmul_rn(c[e], inv);
+      s[e] = __fmul_rn(s[e], inv);
+    }
   }
   const int rows = p.U * p.H;
   const int64_t src_off = slot * p.src_row_stride;
@@ -92,11 +104,13 @@ __global__ void __launch_bounds__(256) derotate_pack_kernel(const __grid_constan
       uint32_t oa[4], ob[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float x0l = bf16_lo(av[e]), x0h = bf16_hi(av[e]);
-        float x1l = bf16_lo(bv[e]), x1h = bf16_hi(bv[e]);
-        float y0l, y1l, y0h, y1h;
-        rope_remove_pair(x0l, x1l, c[2 * e], s[2 * e], y0l, y1l);
-        rope_remove_pair(x0h, x1h, c[2 * e + 1], s[2 * e + 1], y0h, y1h);
+        const float x0l = bf16_lo(av[e]), x0h = bf16_hi(av[e]);
+        const float x1l = bf16_lo(bv[e]), x1h = bf16_hi(bv[e]);
+        // (x0*c + x1*s)/m and (x1*c - x0*s)/m with c, s pre-divided by m.
+        const float y0l = __fmaf_rn(x0l, c[2 * e], __fmul_rn(x1l, s[2 * e]));
+        const float y1l = __fmaf_rn(x1l, c[2 * e], -__fmul_rn(x0l, s[2 * e]));
+        const float y0h = __fmaf_rn(x0h, c[2 * e + 1], __fmul_rn(x1h, s[2 * e + 1]));
+        const float y1h = __fmaf_rn(x1h, c[2 * e + 1], -__fmul_rn(x0h, s[2 * e + 1]));
         oa[e] = pack_bf16x2(y0l, y0h);
         ob[e] = pack_bf16x2(y1l, y1h);
       }
@@ -196,8 +210,8 @@ __global__ void __launch_bounds__(256) map_install_simt_kernel(const __grid_cons
     float x = to_f32<T>(row[e]);
     if (kind == 0) {
       const int i = e < half ? e : e - half;
-      const float c = __ldg(p.scos + t * half + i);
-      const float s = __ldg(p.ssin + t * half + i);
+      float c, s;
+      rope_coeff(static_cast<float>(p.position_start + t), p.src_rope.inv_freq[i], p.src_rope.magnitude, c, s);
       float o0, o1;
       if (e < half) {
         rope_remove_pair(x, to_f32<T>(row[e + half]), c, s, o0, o1);
@@ -228,8 +242,8 @@ __global__ void __launch_bounds__(256) map_install_simt_kernel(const __grid_cons
     float y = Y[idx];
     if (kind == 0) {
       const int i = d < half ? d : d - half;
-      const float c = __ldg(p.dcos + t * half + i);
-      const float s = __ldg(p.dsin + t * half + i);
+      float c, s;
+      rope_coeff(static_cast<float>(p.position_start + t), p.dst_rope.inv_freq[i], p.dst_rope.magnitude, c, s);
       float o0, o1;
       if (d < half) {
         rope_apply_pair(y, Y[idx + half], c, s, o0, o1);

@@ -8,13 +8,12 @@
 namespace cbk {
 
 struct RopeTableParams {
-  float inv_freq[128];
-  int half_dim;
-  float magnitude;
+  RopeDev rope;
   int64_t position_start;
   int64_t n;
-  float* out_cos;
+  float* out_cos;  // [half_dim][out_stride]
   float* out_sin;
+  int64_t out_stride;
 };
 
 struct DerotateParams {
@@ -28,8 +27,8 @@ struct DerotateParams {
   int src_head_offset;
   int src_slot_dtype;
   const void* src_slots;
-  const float* scos;  // [n][64]
-  const float* ssin;
+  RopeDev rope;  // source RoPE
+  int64_t position_start;
   __nv_bfloat16* ws;  // [U][n][H][128]
   int32_t* status;
 };
@@ -70,10 +69,9 @@ struct SimtParams {
   int64_t dst_row_stride, dst_rows;
   int dst_head_offset, dst_slot_dtype;
   const void* dst_slots;
-  const float* scos;  // [n][D/2]
-  const float* ssin;
-  const float* dcos;
-  const float* dsin;
+  RopeDev src_rope;
+  RopeDev dst_rope;
+  int64_t position_start;
   int32_t* status;
 };
 

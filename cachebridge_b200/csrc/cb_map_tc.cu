@@ -8,7 +8,7 @@
 // row straight into the target pool row dst_slots[t]
 // (online/blocks.py:86-111 set_kv_buffer; source_mapper_adapter.py:389-425).
 // Keys read the content-space (source-RoPE-removed, BF16-rounded) rows that
-// cb_derotate.cu packed into the workspace; values read the source pool rows
+// derotate_pack_kernel (cb_kernels.cu) packed into the workspace; values read the source pool rows
 // directly through src_slots (the gather of online/blocks.py:47-82).
 //
 // Work unit ("item"): (head h, kind, chunk of R*128 tokens, target layer l).
@@ -20,17 +20,20 @@
 // CTA (persistent, one per SM, 320 threads) roles:
 //   warps 0-3  producers: 16-byte cp.async gathers of 128 token rows x 256 B
 //              per k-block into a 128B-swizzled K-major stage (ring of NS).
-//   warps 4-7  epilogue: tcgen05.ld of the FP32 accumulator (one token row per
-//              thread), + bias, target RoPE (K), BF16, staging through a
-//              swizzled 8 KB/warp buffer, then row-coalesced 16-byte stores
-//              (two 256-byte rows per warp instruction) to the pool rows.
-//   warp 8     TMEM owner + single-thread tcgen05.mma issuer (M=128, N=128,
+//   warps 4-11 epilogue, two groups of four warps that take alternate
+//              m-tiles; in a group, warp q reads TMEM lane quarter q (token
+//              rows 32q..32q+31, one row per thread). Per 32-pair half row:
+//              two tcgen05.ld rounds of 16 RoPE pairs (columns i and i+64),
+//              + bias, target RoPE (K), BF16, staging into the warp's
+//              swizzled 32 x 128 B tile, then 16-byte stores of 4 rows x
+//              (2 x 64 B) per warp instruction.
+//   warp 12    TMEM owner + single-thread tcgen05.mma issuer (M=128, N=128,
 //              K=16 steps; 8 steps per 128-feature k-block).
-//   warp 9     weight loader: one bulk copy per 32 KB weight k-block (the
+//   warp 13    weight loader: one bulk copy per 32 KB weight k-block (the
 //              pre-swizzled image built at upload); resident for the whole
 //              item when S <= 4, streamed per m-tile otherwise.
-// Accumulators: 2 x (128 lanes x 128 fp32 columns) in TMEM, so the epilogue of
-// m-tile i overlaps the MMAs of m-tile i+1.
+// Accumulators: 4 x (128 lanes x 128 fp32 columns) in TMEM (all 512 columns),
+// so the MMAs run up to three m-tiles ahead of the two epilogue groups.
 #include "cb_device.cuh"
 #include "cb_map_tc.cuh"
 
@@ -42,10 +45,10 @@ constexpr int kBarFull = 0;       // [4]  producers -> MMA (A stage filled)
 constexpr int kBarEmpty = 4;      // [4]  MMA -> producers (A stage consumed)
 constexpr int kBarWFull = 8;      // [4]  loader -> MMA (weight slot filled)
 constexpr int kBarWEmpty = 12;    // [4]  MMA -> loader (weight slot consumed)
-constexpr int kBarAccFull = 16;   // [2]  MMA -> epilogue (accumulator ready)
-constexpr int kBarAccEmpty = 18;  // [2]  epilogue -> MMA (accumulator drained)
-constexpr int kBarDone = 20;      // [1]  MMA drain at exit
-constexpr int kNumBars = 24;
+constexpr int kBarAccFull = 16;   // [4]  MMA -> epilogue (accumulator ready)
+constexpr int kBarAccEmpty = 20;  // [4]  epilogue -> MMA (accumulator drained)
+constexpr int kBarDone = 24;      // [1]  MMA drain at exit
+constexpr int kNumBars = 32;
 
 struct Item {
   int kind;   // 0 = K, 1 = V
@@ -86,22 +89,28 @@ __device__ __forceinline__ uint32_t bar_at(const Smem& s, int idx) { return s.ba
 // ------------------------------- producers ---------------------------------
 __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int lane) {
   const int NS = p.stages;
-  const int LAG = p.stages - 1;
-  int issued = 0, finished = 0;
+  int issued = 0;
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
+    // Slot of this lane's token row, prefetched one m-tile ahead.
+    const int lane_row = pw * 32 + lane;
+    int next_t = it.tok0 + lane_row;
+    int next_valid = next_t < p.n_tokens;
+    int64_t next_row = next_t;
+    if (it.kind == 1 && next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, next_t);
     for (int m = 0; m < it.mtiles && ok; ++m) {
-      // This lane's token row of the m-tile (row = pw*32 + lane).
-      const int t = it.tok0 + m * kBM + pw * 32 + lane;
-      int valid = t < p.n_tokens;
-      int64_t srow = t;
-      if (it.kind == 1 && valid) {
-        srow = load_slot(p.src_slots, p.src_slot_dtype, t);
-        if (srow < 0 || srow >= p.src_rows) {
-          flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-          valid = 0;
-        }
+      int valid = next_valid;
+      int64_t srow = next_row;
+      if (m + 1 < it.mtiles) {
+        next_t += kBM;
+        next_valid = next_t < p.n_tokens;
+        next_row = next_t;
+        if (it.kind == 1 && next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, next_t);
+      }
+      if (it.kind == 1 && valid && (srow < 0 || srow >= p.src_rows)) {
+        flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+        valid = 0;
       }
       for (int j = 0; j < p.S; ++j) {
         const int stage = issued % NS;
@@ -138,24 +147,15 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
               stage_addr + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4);
           cp_async_16(dst, g, vv ? 16u : 0u);
         }
-        cp_async_commit();
+        // The stage's full barrier (count 128) completes when every producer
+        // thread's copies have landed, independently of the producer's progress.
+        cp_async_arrive_noinc(bar_at(s, kBarFull + stage));
         ++issued;
-        if (issued - finished > LAG) {
-          cp_async_wait_dyn(LAG);
-          fence_proxy_async_smem();
-          mbar_arrive(bar_at(s, kBarFull + (finished % NS)));
-          ++finished;
-        }
       }
     }
   }
-  // Drain: every issued group completes (plain loads always finish).
-  cp_async_wait<0>();
-  fence_proxy_async_smem();
-  while (finished < issued) {
-    mbar_arrive(bar_at(s, kBarFull + (finished % NS)));
-    ++finished;
-  }
+  // Never exit with copies in flight into shared memory.
+  cp_async_wait_all();
 }
 
 // ------------------------------ weight loader ------------------------------
@@ -221,8 +221,8 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
     for (int m = 0; m < it.mtiles && ok; ++m) {
-      const int acc = accc & 1;
-      if (!mbar_wait(bar_at(s, kBarAccEmpty + acc), ((accc >> 1) & 1) ^ 1, s.abort_flag,
+      const int acc = accc & 3;
+      if (!mbar_wait(bar_at(s, kBarAccEmpty + acc), ((accc >> 2) & 1) ^ 1, s.abort_flag,
                      p.status)) {
         ok = false;
         break;
@@ -288,122 +288,146 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
 }
 
 // -------------------------------- epilogue ---------------------------------
-__device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int eq,
+__device__ __forceinline__ void load16(const float* src, float (&out)[16]) {
+  const float4* v = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = __ldg(v + q);
+    out[4 * q + 0] = x.x;
+    out[4 * q + 1] = x.y;
+    out[4 * q + 2] = x.z;
+    out[4 * q + 3] = x.w;
+  }
+}
+
+// Warp (group g, quarter eq): m-tiles n with n % 2 == g, token rows eq*32 + lane.
+// Target RoPE coefficients come from the frequency-major table [64][n] that
+// phase 1 wrote: one load instruction fetches one frequency for the warp's 32
+// consecutive tokens (one 128-byte line); the next round's 16 are fetched while
+// the current round computes.
+__device__ __forceinline__ void load_rope16(const float* cos_row0, const float* sin_row0, int64_t rs,
+                                            float (&c)[16], float (&s)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    c[e] = __ldg(cos_row0 + e * rs);
+    s[e] = __ldg(sin_row0 + e * rs);
+  }
+}
+
+__device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int g, int eq,
                              int lane) {
-  uint8_t* stage_gen = s.e_gen + eq * kEpiWarpBytes;
-  const uint32_t stage_s = s.e + eq * kEpiWarpBytes;
-  int accc = 0;
+  uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 128 B, this warp only
+  uint8_t* my_row = stage + lane * 128;
+  const int64_t dst_stride_bytes = p.dst_row_stride * 2;
+  const int64_t rs = p.n_tokens;
+  int accc = 0;  // CTA-wide m-tile counter (both groups count every m-tile)
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
     const float* bias = p.bias + (static_cast<int64_t>(it.kind * p.L_t + it.l) * p.H + it.h) * kD;
     char* dst_layer = reinterpret_cast<char*>(it.kind ? p.dst_v[it.l] : p.dst_k[it.l]) +
                       static_cast<int64_t>(p.dst_head_offset + it.h) * (kD * 2);
-    const int64_t dst_stride_bytes = p.dst_row_stride * 2;
-    for (int m = 0; m < it.mtiles; ++m) {
-      const int acc = accc & 1;
+    for (int m = 0; m < it.mtiles; ++m, ++accc) {
+      if ((accc & 1) != g) continue;
+      const int t = it.tok0 + m * kBM + eq * 32 + lane;
+      int valid = t < p.n_tokens;
+      int64_t dslot = valid ? load_slot(p.dst_slots, p.dst_slot_dtype, t) : 0;
+      if (valid && (dslot < 0 || dslot >= p.dst_rows)) {
+        flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+        valid = 0;
+      }
+      const bool do_rope = it.kind == 0 && valid;
+      const float* cbase = p.dcos + t;
+      const float* sbase = p.dsin + t;
+      float ca[16], sa[16];  // coefficients of the current 16-pair round
+      if (do_rope) load_rope16(cbase, sbase, rs, ca, sa);
+      const int acc = accc & 3;
       // Warp-uniform outcome: tcgen05.ld is .sync.aligned across the warp.
-      const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (accc >> 1) & 1, s.abort_flag, p.status);
+      const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (accc >> 2) & 1, s.abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int row = eq * 32 + lane;
-      const int t = it.tok0 + m * kBM + row;
-      int valid = t < p.n_tokens;
-      int64_t dslot = 0;
-      if (valid) {
-        dslot = load_slot(p.dst_slots, p.dst_slot_dtype, t);
-        if (dslot < 0 || dslot >= p.dst_rows) {
-          flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-          valid = 0;
-        }
-      }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(eq * 32) << 16) + acc * kD;
-      uint8_t* my_row = stage_gen + lane * 256;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t lo[32], hi[32];
-        tmem_ld_32x32b_x32(tbase + half * 32, lo);
-        tmem_ld_32x32b_x32(tbase + 64 + half * 32, hi);
-        tmem_wait_ld();
-        if (half == 1) {
-          // Accumulator fully read into registers: hand it back to the MMA.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
-        }
-        float ylo[32], yhi[32];
+      for (int hb = 0; hb < 2; ++hb) {  // RoPE pairs [32hb, 32hb+32)
 #pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + half * 32) + q4);
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + 64 + half * 32) + q4);
-          ylo[4 * q4 + 0] = __fadd_rn(__uint_as_float(lo[4 * q4 + 0]), b0.x);
-          ylo[4 * q4 + 1] = __fadd_rn(__uint_as_float(lo[4 * q4 + 1]), b0.y);
-          ylo[4 * q4 + 2] = __fadd_rn(__uint_as_float(lo[4 * q4 + 2]), b0.z);
-          ylo[4 * q4 + 3] = __fadd_rn(__uint_as_float(lo[4 * q4 + 3]), b0.w);
-          yhi[4 * q4 + 0] = __fadd_rn(__uint_as_float(hi[4 * q4 + 0]), b1.x);
-          yhi[4 * q4 + 1] = __fadd_rn(__uint_as_float(hi[4 * q4 + 1]), b1.y);
-          yhi[4 * q4 + 2] = __fadd_rn(__uint_as_float(hi[4 * q4 + 2]), b1.z);
-          yhi[4 * q4 + 3] = __fadd_rn(__uint_as_float(hi[4 * q4 + 3]), b1.w);
-        }
-        if (it.kind == 0 && valid) {
-          const float4* cp = reinterpret_cast<const float4*>(p.dcos + static_cast<int64_t>(t) * 64 + half * 32);
-          const float4* sp = reinterpret_cast<const float4*>(p.dsin + static_cast<int64_t>(t) * 64 + half * 32);
+        for (int sr = 0; sr < 2; ++sr) {  // 16-pair round
+          const int p0 = 32 * hb + 16 * sr;  // first pair of the round
+          uint32_t lo[16], hi[16];
+          tmem_ld_32x32b_x16(tbase + p0, lo);
+          tmem_ld_32x32b_x16(tbase + 64 + p0, hi);
+          float cb[16], sb[16];  // next round's coefficients, fetched while this one computes
+          const bool prefetch = do_rope && p0 + 16 < 64;
+          if (prefetch) load_rope16(cbase + (p0 + 16) * rs, sbase + (p0 + 16) * rs, rs, cb, sb);
+          tmem_wait_ld();
+          if (hb == 1 && sr == 1) {
+            // Accumulator fully read into registers: hand it back to the MMA.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
+          }
+          float blo[16], bhi[16];
+          load16(bias + p0, blo);
+          load16(bias + 64 + p0, bhi);
+          float ylo[16], yhi[16];
 #pragma unroll
-          for (int q4 = 0; q4 < 8; ++q4) {
-            const float4 c4 = __ldg(cp + q4);
-            const float4 s4 = __ldg(sp + q4);
-            const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-            const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+          for (int e = 0; e < 16; ++e) {
+            ylo[e] = __fadd_rn(__uint_as_float(lo[e]), blo[e]);
+            yhi[e] = __fadd_rn(__uint_as_float(hi[e]), bhi[e]);
+          }
+          if (do_rope) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
+            for (int e = 0; e < 16; ++e) {
               float o0, o1;
-              rope_apply_pair(ylo[4 * q4 + e], yhi[4 * q4 + e], cc[e], ss[e], o0, o1);
-              ylo[4 * q4 + e] = o0;
-              yhi[4 * q4 + e] = o1;
+              rope_apply_pair(ylo[e], yhi[e], ca[e], sa[e], o0, o1);
+              ylo[e] = o0;
+              yhi[e] = o1;
             }
           }
-        }
-        // Stage this thread's row: logical 16-byte chunk c of the 256-byte row
-        // sits at physical chunk (c & 8) | ((c & 7) ^ (lane & 7)).
+          if (prefetch) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 vlo, vhi;
-          vlo.x = pack_bf16x2(ylo[8 * k + 0], ylo[8 * k + 1]);
-          vlo.y = pack_bf16x2(ylo[8 * k + 2], ylo[8 * k + 3]);
-          vlo.z = pack_bf16x2(ylo[8 * k + 4], ylo[8 * k + 5]);
-          vlo.w = pack_bf16x2(ylo[8 * k + 6], ylo[8 * k + 7]);
-          vhi.x = pack_bf16x2(yhi[8 * k + 0], yhi[8 * k + 1]);
-          vhi.y = pack_bf16x2(yhi[8 * k + 2], yhi[8 * k + 3]);
-          vhi.z = pack_bf16x2(yhi[8 * k + 4], yhi[8 * k + 5]);
-          vhi.w = pack_bf16x2(yhi[8 * k + 6], yhi[8 * k + 7]);
-          const int clo = half * 4 + k;       // chunks 0..7
-          const int chi = 8 + half * 4 + k;   // chunks 8..15
-          *reinterpret_cast<uint4*>(my_row + ((((clo & 7) ^ (lane & 7))) << 4)) = vlo;
-          *reinterpret_cast<uint4*>(my_row + ((8 | ((chi & 7) ^ (lane & 7))) << 4)) = vhi;
+            for (int e = 0; e < 16; ++e) {
+              ca[e] = cb[e];
+              sa[e] = sb[e];
+            }
+          }
+          // Local chunk lc of the warp's 128-byte row piece: 0-3 = columns
+          // [32hb, 32hb+32), 4-7 = [64+32hb, ...); it sits at lc ^ (row & 7).
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            uint4 vlo, vhi;
+            vlo.x = pack_bf16x2(ylo[8 * k + 0], ylo[8 * k + 1]);
+            vlo.y = pack_bf16x2(ylo[8 * k + 2], ylo[8 * k + 3]);
+            vlo.z = pack_bf16x2(ylo[8 * k + 4], ylo[8 * k + 5]);
+            vlo.w = pack_bf16x2(ylo[8 * k + 6], ylo[8 * k + 7]);
+            vhi.x = pack_bf16x2(yhi[8 * k + 0], yhi[8 * k + 1]);
+            vhi.y = pack_bf16x2(yhi[8 * k + 2], yhi[8 * k + 3]);
+            vhi.z = pack_bf16x2(yhi[8 * k + 4], yhi[8 * k + 5]);
+            vhi.w = pack_bf16x2(yhi[8 * k + 6], yhi[8 * k + 7]);
+            const int llo = 2 * sr + k;
+            const int lhi = 4 + 2 * sr + k;
+            *reinterpret_cast<uint4*>(my_row + ((llo ^ (lane & 7)) << 4)) = vlo;
+            *reinterpret_cast<uint4*>(my_row + ((lhi ^ (lane & 7)) << 4)) = vhi;
+          }
         }
-      }
-      __syncwarp();
-      // Row-coalesced stores: lanes 0-15 write row 2i, lanes 16-31 row 2i+1.
-      const int c = lane & 15;
-#pragma unroll 4
-      for (int ii = 0; ii < 16; ++ii) {
-        const int r = 2 * ii + (lane >> 4);
-        const int64_t sl = __shfl_sync(0xffffffffu, dslot, r);
-        const int vv = __shfl_sync(0xffffffffu, valid, r);
-        const uint4 v = *reinterpret_cast<const uint4*>(stage_gen + r * 256 +
-                                                        (((c & 8) | ((c & 7) ^ (r & 7))) << 4));
-        if (vv) {
-          *reinterpret_cast<uint4*>(dst_layer + sl * dst_stride_bytes + c * 16) = v;
+        __syncwarp();
+        // Stores: 4 rows x (2 x 64 contiguous bytes) per warp instruction.
+        const int lc = lane & 7;
+        const int gchunk = lc < 4 ? 4 * hb + lc : 8 + 4 * hb + (lc - 4);
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+          const int rr = 4 * ii + (lane >> 3);
+          const int64_t sl = __shfl_sync(0xffffffffu, dslot, rr);
+          const int vv = __shfl_sync(0xffffffffu, valid, rr);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((lc ^ (rr & 7)) << 4));
+          if (vv) *reinterpret_cast<uint4*>(dst_layer + sl * dst_stride_bytes + gchunk * 16) = v;
         }
+        __syncwarp();
       }
-      __syncwarp();
-      ++accc;
     }
   }
-  (void)stage_s;
 }
 
 }  // namespace
@@ -420,7 +444,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
   s.a = base + p.w_slots * kKBlockBytes;
   s.e = s.a + p.stages * kKBlockBytes;
   s.e_gen = base_gen + (s.e - base);
-  s.bars = s.e + 4 * kEpiWarpBytes;
+  s.bars = s.e + kEpiWarps * kEpiWarpBytes;
   uint8_t* bars_gen = base_gen + (s.bars - base);
   s.tmem_holder = reinterpret_cast<uint32_t*>(bars_gen + 8 * kNumBars);
   s.abort_flag = reinterpret_cast<volatile int*>(bars_gen + 8 * kNumBars + 4);
@@ -437,16 +461,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
       mbar_init(bar_at(s, kBarWFull + i), 1);
       mbar_init(bar_at(s, kBarWEmpty + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(bar_at(s, kBarAccFull + i), 1);
-      mbar_init(bar_at(s, kBarAccEmpty + i), 4);
+      mbar_init(bar_at(s, kBarAccEmpty + i), 4);  // the 4 warps of the group that owns the m-tile
     }
     mbar_init(bar_at(s, kBarDone), 1);
     *s.abort_flag = 0;
     fence_mbarrier_init();
     fence_proxy_async_smem();
   }
-  if (warp == 8) {
+  constexpr int kMmaWarp = 4 + kEpiWarps;
+  constexpr int kLoaderWarp = kMmaWarp + 1;
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(s.tmem_holder), kTmemCols);
     tmem_relinquish();
   }
@@ -457,19 +483,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
 
   if (warp < 4) {
     run_producer(p, s, warp, lane);
-  } else if (warp < 8) {
-    run_epilogue(p, s, tmem_base, warp - 4, lane);
-  } else if (warp == 8) {
+  } else if (warp < kMmaWarp) {
+    // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule); group = (warp - 4) / 4.
+    run_epilogue(p, s, tmem_base, (warp - 4) >> 2, warp & 3, lane);
+  } else if (warp == kMmaWarp) {
     if (lane == 0) run_mma(p, s, tmem_base);
     __syncwarp();
-  } else {
+  } else if (warp == kLoaderWarp) {
     if (lane == 0) run_weight_loader(p, s);
     __syncwarp();
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

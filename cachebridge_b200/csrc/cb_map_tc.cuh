@@ -11,9 +11,11 @@ constexpr int kD = 128;                        // head_dim of the tensor-core pa
 constexpr int kBM = 128;                       // tokens per m-tile (UMMA M)
 constexpr int kPanelBytes = 128 * 128;         // 128 rows x 64 bf16 (one 128B-swizzle panel)
 constexpr int kKBlockBytes = 2 * kPanelBytes;  // 128 rows x 128 bf16: one source layer's head
-constexpr int kEpiWarpBytes = 32 * 256;        // 32 token rows x 256 B staging per epilogue warp
-constexpr int kTcThreads = 320;                // 4 producer + 4 epilogue + MMA + loader warps
-constexpr int kTmemCols = 256;                 // two 128-column FP32 accumulators
+constexpr int kEpiWarps = 8;                   // two groups of 4 (one warp per TMEM lane quarter)
+constexpr int kEpiWarpBytes = 32 * 128;        // 32 token rows x 128 B staging per epilogue warp
+constexpr int kAccBufs = 4;                    // FP32 accumulators in TMEM (128 columns each)
+constexpr int kTcThreads = 32 * (4 + kEpiWarps + 2);  // producers, epilogue, MMA, loader
+constexpr int kTmemCols = 128 * kAccBufs;      // all 512 TMEM columns
 constexpr int kTcMaxSmem = 232448;             // sm_100 opt-in dynamic shared memory per block
 
 struct MapTcParams {
@@ -49,7 +51,7 @@ struct MapTcParams {
   int dst_slot_dtype;
   const void* dst_slots;
 
-  const float* dcos;  // [n_tokens][64] target RoPE
+  const float* dcos;  // [64][n_tokens] target RoPE coefficients (workspace tail)
   const float* dsin;
   int32_t* status;
 };
@@ -58,8 +60,8 @@ __global__ void map_install_tc_kernel(const __grid_constant__ MapTcParams p);
 
 // Shared-memory bytes the kernel needs for a given weight-slot / stage split.
 inline int tc_smem_bytes(int w_slots, int stages) {
-  return 1024 /* alignment slack */ + (w_slots + stages) * kKBlockBytes + 4 * kEpiWarpBytes +
-         256 /* barriers, TMEM holder, abort flag */;
+  return 1024 /* alignment slack */ + (w_slots + stages) * kKBlockBytes + kEpiWarps * kEpiWarpBytes +
+         512 /* barriers, TMEM holder, abort flag */;
 }
 
 }  // namespace cbk

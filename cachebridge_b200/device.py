@@ -149,7 +149,9 @@ def status_word(device: torch.device) -> torch.Tensor:
     key = torch.device(device).index
     word = _status_words.get(key)
     if word is None:
-        word = torch.zeros(1, dtype=torch.int32, device=device)
+        # A normal (non-inference) tensor, so it can be cleared in or out of inference mode.
+        with torch.inference_mode(False):
+            word = torch.zeros(1, dtype=torch.int32, device=device)
         _status_words[key] = word
     return word
 
@@ -173,6 +175,17 @@ def raise_for_status(device: torch.device) -> None:
         raise RuntimeError(f"handoff kernel reported device status {bits}")
 
 
+def rope_descriptor(head_dim: int, theta: float, scaling: dict | None) -> nat.CbRope:
+    """``cb_rope`` for a model's RoPE (inv_freq and YaRN magnitude, rope.py:16-69)."""
+    inv_freq, magnitude = rope_parameters(head_dim, theta, scaling)
+    rope = nat.CbRope()
+    rope.half_dim = head_dim // 2
+    rope.magnitude = magnitude
+    for i, v in enumerate(inv_freq.tolist()):
+        rope.inv_freq[i] = v
+    return rope
+
+
 def rope_tables(
     device: torch.device,
     head_dim: int,
@@ -181,23 +194,22 @@ def rope_tables(
     position_start: int,
     n: int,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """cos/sin tables [n, head_dim/2] (FP32) for positions position_start..+n-1."""
+    """Frequency-major cos/sin tables ``[head_dim/2, n]`` (FP32) for positions
+    ``position_start .. +n-1`` (entry ``[i, t]`` is frequency i of token t)."""
     lib = nat.load()
-    inv_freq, magnitude = rope_parameters(head_dim, theta, scaling)
-    half = head_dim // 2
-    cos = torch.empty((max(n, 1), half), dtype=torch.float32, device=device)
+    rope = rope_descriptor(head_dim, theta, scaling)
+    width = max(n, 1)
+    cos = torch.empty((head_dim // 2, width), dtype=torch.float32, device=device)
     sin = torch.empty_like(cos)
-    arr = (ctypes.c_float * half)(*inv_freq.tolist())
     nat.check(
         lib.cb_rope_table(
             ctypes.c_void_p(current_stream_ptr(device)),
-            arr,
-            half,
-            ctypes.c_float(magnitude),
+            ctypes.byref(rope),
             int(position_start),
             int(n),
             cos.data_ptr(),
             sin.data_ptr(),
+            width,
         ),
         "cb_rope_table",
     )

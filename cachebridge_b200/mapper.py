@@ -20,7 +20,7 @@ import torch
 from safetensors.torch import load_file
 
 from . import _native as nat
-from .device import RowSet, require_cuda, rope_tables, status_word, storage_dtype_code, current_stream_ptr
+from .device import RowSet, current_stream_ptr, rope_descriptor, status_word, storage_dtype_code
 
 
 @dataclass(frozen=True)
@@ -237,7 +237,7 @@ class PageMapper:
         n = int(n_tokens)
         if (src.slots is not None and src.slots.numel() < n) or (dst.slots is not None and dst.slots.numel() < n):
             raise ValueError("invalid target range or non-CacheBridge method")
-        return HandoffCall(self, src, dst, n, int(position_start), tables=tables, workspace=workspace)
+        return HandoffCall(self, src, dst, n, int(position_start), workspace=workspace)
 
     def map_install(self, src: RowSet, dst: RowSet, n_tokens: int, position_start: int) -> None:
         """Fused gather + map + install of ``n_tokens`` tokens.
@@ -305,7 +305,7 @@ class HandoffCall:
     """One prepared ``cb_map_install`` (or its two phases) with marshalled arguments."""
 
     def __init__(self, mapper: PageMapper, src: RowSet, dst: RowSet, n: int, position_start: int, *,
-                 tables=None, workspace=None):
+                 workspace=None):
         self.mapper = mapper
         self.n = n
         self.position_start = position_start
@@ -313,18 +313,9 @@ class HandoffCall:
         self.src_c, self.dst_c = src.to_c(), dst.to_c()
         self.dtype = storage_dtype_code(src.dtype)
         self.tensor_core = mapper.head_dim == 128 and src.dtype == torch.bfloat16
-        self.same_rope = (mapper.target_rope_theta, mapper.target_rope_scaling) == (
-            mapper.source_rope_theta,
-            mapper.source_rope_scaling,
-        )
+        self.src_rope = rope_descriptor(mapper.head_dim, mapper.source_rope_theta, mapper.source_rope_scaling)
+        self.dst_rope = rope_descriptor(mapper.head_dim, mapper.target_rope_theta, mapper.target_rope_scaling)
         dev = mapper.device
-        if tables is not None:
-            self.scos, self.ssin, self.dcos, self.dsin = tables
-            for t in tables:
-                if t.dtype != torch.float32 or t.device != dev or t.shape[0] < n or not t.is_contiguous():
-                    raise ValueError("RoPE tables must be contiguous FP32 [n, head_dim/2] on the mapper device")
-        elif n:
-            self.refresh_tables()
         ws_bytes = mapper.workspace_bytes(src.dtype, n)
         if workspace is None:
             workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
@@ -332,20 +323,6 @@ class HandoffCall:
             raise ValueError("workspace missing, too small or on the wrong device")
         self.workspace = workspace
         self.status = status_word(dev)
-
-    def refresh_tables(self) -> int:
-        """(Re)build the RoPE tables on the current stream; returns kernel launches."""
-        m = self.mapper
-        self.scos, self.ssin = rope_tables(
-            m.device, m.head_dim, m.source_rope_theta, m.source_rope_scaling, self.position_start, self.n
-        )
-        if self.same_rope:
-            self.dcos, self.dsin = self.scos, self.ssin
-            return 1
-        self.dcos, self.dsin = rope_tables(
-            m.device, m.head_dim, m.target_rope_theta, m.target_rope_scaling, self.position_start, self.n
-        )
-        return 2
 
     def _stream(self):
         return ctypes.c_void_p(current_stream_ptr(self.mapper.device))
@@ -357,19 +334,20 @@ class HandoffCall:
         nat.check(
             nat.load().cb_map_install(
                 self.mapper._handle, self._stream(), ctypes.byref(self.src_c), ctypes.byref(self.dst_c), self.n,
-                self.scos.data_ptr(), self.ssin.data_ptr(), self.dcos.data_ptr(), self.dsin.data_ptr(),
-                self.dtype, self.workspace.data_ptr(), self.workspace.numel(), self.status.data_ptr(),
+                self.position_start, ctypes.byref(self.src_rope), ctypes.byref(self.dst_rope), self.dtype,
+                self.workspace.data_ptr(), self.workspace.numel(), self.status.data_ptr(),
             ),
             "cb_map_install",
         )
 
     def derotate(self) -> None:
-        """Phase 1 of the tensor-core path (``cb_derotate_keys``)."""
+        """Phase 1 of the tensor-core path (``cb_derotate_keys``): content-space
+        keys and the target RoPE coefficients into the workspace."""
         nat.check(
             nat.load().cb_derotate_keys(
-                self.mapper._handle, self._stream(), ctypes.byref(self.src_c), self.n,
-                self.scos.data_ptr(), self.ssin.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
-                self.status.data_ptr(),
+                self.mapper._handle, self._stream(), ctypes.byref(self.src_c), self.n, self.position_start,
+                ctypes.byref(self.src_rope), ctypes.byref(self.dst_rope), self.workspace.data_ptr(),
+                self.workspace.numel(), self.status.data_ptr(),
             ),
             "cb_derotate_keys",
         )
@@ -379,8 +357,7 @@ class HandoffCall:
         nat.check(
             nat.load().cb_map_install_packed(
                 self.mapper._handle, self._stream(), ctypes.byref(self.src_c), ctypes.byref(self.dst_c), self.n,
-                self.dcos.data_ptr(), self.dsin.data_ptr(), self.workspace.data_ptr(), self.workspace.numel(),
-                self.status.data_ptr(),
+                self.workspace.data_ptr(), self.workspace.numel(), self.status.data_ptr(),
             ),
             "cb_map_install_packed",
         )

@@ -14,8 +14,9 @@
  *  - Return value: CB_OK (0) or a negative CB_ERR_* code. No call throws across
  *    the ABI. cb_last_error() returns a thread-local message for the last
  *    failure on the calling thread.
- *  - Hot-path calls (cb_map_install, cb_pack_rows, cb_install_rows,
- *    cb_rope_table) never allocate device or host memory. cb_mapper_create is
+ *  - Hot-path calls (cb_map_install, cb_derotate_keys, cb_map_install_packed,
+ *    cb_pack_rows, cb_install_rows, cb_rope_table) never allocate device or
+ *    host memory. cb_mapper_create is
  *    the only allocating call besides the IPC helpers.
  *  - Row indices (slots) are validated on the device: an index outside
  *    [0, rows) is skipped and CB_DEV_ERR_SLOT_RANGE is OR-ed into the caller's
@@ -78,6 +79,21 @@ typedef struct cb_rows {
   const void* slots;       /* device [n_tokens] row indices, or NULL */
 } cb_rows;
 
+/*
+ * Split-half (Qwen) RoPE of one model. Token t of a call sits at absolute
+ * position position_start + t; frequency i < half_dim has the FP32 phase
+ * float(position) * inv_freq[i] and the coefficients cos(phase) * magnitude,
+ * sin(phase) * magnitude: the table of qwen_rope (src/cachebridge/rope.py:16-72),
+ * whose cat(phase, phase) duplicate half is implied. inv_freq and magnitude
+ * (YaRN included, rope.py:28-69) are computed by the caller; the kernels
+ * evaluate the coefficients themselves, so no table crosses the ABI.
+ */
+typedef struct cb_rope {
+  int32_t half_dim;      /* head_dim / 2, at most 128 */
+  float magnitude;       /* YaRN attention magnitude, 1.0 without scaling */
+  float inv_freq[128];   /* first half_dim entries used */
+} cb_rope;
+
 typedef struct cb_mapper cb_mapper;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -115,15 +131,15 @@ CB_API size_t cb_mapper_workspace_bytes(const cb_mapper* mapper, int dtype,
                                  int64_t n_tokens);
 
 /*
- * Split-half (Qwen) RoPE tables for positions position_start .. +n-1:
- *   cos[t][i] = cos(float(p_t) * inv_freq[i]) * magnitude, sin likewise,
- * i < half_dim. inv_freq is a HOST array [half_dim] (at most 128 values).
- * Replaces qwen_rope (src/cachebridge/rope.py:16-72), whose cat(phase, phase)
- * duplicate half is implied. Outputs are device [n][half_dim] FP32.
+ * RoPE coefficient tables (a utility; the handoff kernels do not need them):
+ * for i < rope->half_dim and t < n,
+ *   out_cos[i * out_stride + t] = cos(float(position_start + t) * inv_freq[i]) * magnitude
+ * and out_sin likewise, out_stride >= n (frequency-major). Equals
+ * qwen_rope (src/cachebridge/rope.py:16-72) transposed, without its
+ * duplicated second half.
  */
-CB_API int cb_rope_table(void* stream, const float* inv_freq, int half_dim,
-                  float magnitude, int64_t position_start, int64_t n,
-                  float* out_cos, float* out_sin);
+CB_API int cb_rope_table(void* stream, const cb_rope* rope, int64_t position_start,
+                  int64_t n, float* out_cos, float* out_sin, int64_t out_stride);
 
 /*
  * Fused pack + mapper apply + install for n_tokens tokens.
@@ -137,8 +153,10 @@ CB_API int cb_rope_table(void* stream, const float* inv_freq, int half_dim,
  *   dst: target rows, dst->layers == target_layers; token t of target head h
  *        is written to row dst->slots[t], head dst->head_offset + h. dst
  *        pointers may be peer-device pointers (CUDA IPC / peer access).
- *   src_cos/src_sin, dst_cos/dst_sin: cb_rope_table outputs for the tokens'
- *        absolute positions (source and target RoPE).
+ *   position_start: absolute position of token 0 of this call (token t is at
+ *        position_start + t, mapper.py:131-136).
+ *   src_rope, dst_rope: source and target model RoPE (mapper.py:137-142,
+ *        209-214).
  *   dtype: storage dtype of src and dst rows (CB_DTYPE_BF16 or CB_DTYPE_F32).
  *   workspace: >= cb_mapper_workspace_bytes(mapper, dtype, n_tokens) bytes.
  *   dev_status: device int32 status word (CB_DEV_ERR_* bits are OR-ed in).
@@ -149,9 +167,8 @@ CB_API int cb_rope_table(void* stream, const float* inv_freq, int half_dim,
  * (BF16 operands, FP32 accumulation); other geometries on a CUDA-core kernel.
  */
 CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
-                   const cb_rows* dst, int64_t n_tokens, const float* src_cos,
-                   const float* src_sin, const float* dst_cos,
-                   const float* dst_sin, int dtype, void* workspace,
+                   const cb_rows* dst, int64_t n_tokens, int64_t position_start,
+                   const cb_rope* src_rope, const cb_rope* dst_rope, int dtype, void* workspace,
                    size_t workspace_bytes, int32_t* dev_status);
 
 /*
@@ -161,18 +178,19 @@ CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
  *  cb_derotate_keys: gather the source key rows of every used source layer
  *    through src->slots, remove the source RoPE in FP32 (rope.py:82-89,
  *    mapper.py:143-144) and store BF16 content-space keys in `workspace`
- *    ([used_layers][n_tokens][heads][128]).
+ *    ([used_layers][n_tokens][heads][128]); also store the target RoPE
+ *    coefficients of the call's positions in the workspace tail.
  *  cb_map_install_packed: map keys from `workspace` and values from the
  *    source rows, apply bias and target RoPE, and install into dst rows.
  * cb_map_install(...) == cb_derotate_keys(...) then cb_map_install_packed(...)
- * on the same stream.
+ * on the same stream, with the same workspace.
  */
 CB_API int cb_derotate_keys(cb_mapper* mapper, void* stream, const cb_rows* src,
-                     int64_t n_tokens, const float* src_cos, const float* src_sin,
-                     void* workspace, size_t workspace_bytes, int32_t* dev_status);
+                     int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
+                     const cb_rope* dst_rope, void* workspace, size_t workspace_bytes,
+                     int32_t* dev_status);
 CB_API int cb_map_install_packed(cb_mapper* mapper, void* stream, const cb_rows* src,
-                          const cb_rows* dst, int64_t n_tokens, const float* dst_cos,
-                          const float* dst_sin, const void* workspace,
+                          const cb_rows* dst, int64_t n_tokens, const void* workspace,
                           size_t workspace_bytes, int32_t* dev_status);
 
 /*

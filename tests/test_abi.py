@@ -42,12 +42,11 @@ def test_version_and_status_strings():
 
 def test_argument_validation_without_gpu():
     lib = nat.load()
-    inv = (ctypes.c_float * 64)()
-    # half_dim out of range: rejected before any CUDA call.
-    rc = lib.cb_rope_table(None, inv, 0, ctypes.c_float(1.0), 0, 4, None, None)
+    rope = nat.CbRope()  # half_dim 0: rejected before any CUDA call
+    rc = lib.cb_rope_table(None, ctypes.byref(rope), 0, 4, None, None, 4)
     assert rc == nat.CB_ERR_INVALID
     assert b"rope table" in lib.cb_last_error()
-    rc = lib.cb_map_install(None, None, None, None, 0, None, None, None, None, 1, None, 0, None)
+    rc = lib.cb_map_install(None, None, None, None, 0, 0, None, None, 1, None, 0, None)
     assert rc == nat.CB_ERR_INVALID
     out = ctypes.c_void_p()
     rc = lib.cb_mapper_create(ctypes.byref(out), 0, 0, 1, 128, 1, None, None, None, None, None)

@@ -302,3 +302,22 @@ def test_map_write_block_installs_packed_block(cuda_device):
     layers, head_range = orc.load_layers(d, tp_rank=1, tp_size=2)
     f32 = orc.map_page_f32(layers, t["page"], head_range=head_range, **oracle_kwargs(params))
     _check_install(pool, t["slots"][:n], f32, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize(
+    "theta,scaling,start",
+    [
+        (1e6, None, 0),
+        (1e4, None, 32000),
+        (1e6, {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 32768}, 40000),
+    ],
+)
+def test_rope_table_matches_qwen_rope(cuda_device, theta, scaling, start):
+    from cachebridge_b200.device import rope_tables
+
+    n, D = 257, 128
+    cos, sin = rope_tables(cuda_device, D, theta, scaling, start, n)
+    ref_cos, ref_sin = orc.qwen_rope(torch.arange(start, start + n), head_dim=D, theta=theta, scaling=scaling)
+    # frequency-major [D/2, n] against the reference's [n, D] (first half)
+    torch.testing.assert_close(cos.cpu().T, ref_cos[:, : D // 2], atol=2e-6, rtol=0)
+    torch.testing.assert_close(sin.cpu().T, ref_sin[:, : D // 2], atol=2e-6, rtol=0)
