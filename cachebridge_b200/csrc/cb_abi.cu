@@ -4,7 +4,9 @@
 // packs kernel parameter blocks and launches on the caller's stream. Hot-path
 // entry points allocate nothing; cb_mapper_create owns all device memory of a
 // mapper. Errors are reported by status code plus a thread-local message.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -94,6 +96,32 @@ int check_rope(const cb_rope* r, int head_dim, const char* name) {
   return CB_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda directly).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }();
+  return fn;
+}
+
+int encode_bf16_map(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                    const cuuint32_t* box) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(CB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box,
+                   elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CB_ERR_INVALID, "cuTensorMapEncodeTiled rejected a map (error " + std::to_string(r) + ")");
+  return CB_OK;
+}
+
 cbk::RopeDev rope_dev(const cb_rope* r) {
   cbk::RopeDev d{};
   std::memcpy(d.inv_freq, r->inv_freq, sizeof(float) * r->half_dim);
@@ -123,20 +151,16 @@ namespace {
 int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
                     size_t workspace_bytes);
 
-// Tensor-core workspace: BF16 content-space keys [U][n][H][128], then the
-// target RoPE coefficient tables cos [64][n] and sin [64][n] (FP32), 256-byte aligned.
-size_t ws_keys_bytes(const cb_mapper* m, int64_t n) {
-  return (static_cast<size_t>(m->U) * static_cast<size_t>(n) * m->H * cbk::kD * 2 + 255) & ~size_t(255);
+// Tensor-core workspace: BF16 content-space keys [U][n][H][128].
+size_t ws_total_bytes(const cb_mapper* m, int64_t n) {
+  return static_cast<size_t>(m->U) * static_cast<size_t>(n) * m->H * cbk::kD * 2;
 }
-size_t ws_table_bytes(int64_t n) { return (static_cast<size_t>(n) * 64 * 4 + 255) & ~size_t(255); }
-size_t ws_total_bytes(const cb_mapper* m, int64_t n) { return ws_keys_bytes(m, n) + 2 * ws_table_bytes(n); }
 
 int launch_rope_table(cudaStream_t st, const cb_rope* rope, int64_t position_start, int64_t n, float* out_cos,
                       float* out_sin, int64_t out_stride);
 
 int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int64_t n_tokens,
-                    int64_t position_start, const cb_rope* src_rope, const cb_rope* dst_rope, void* workspace,
-                    int32_t* dev_status) {
+                    int64_t position_start, const cb_rope* src_rope, void* workspace, int32_t* dev_status) {
   cbk::DerotateParams dp{};
   dp.n_tokens = n_tokens;
   dp.H = m->H;
@@ -156,13 +180,12 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
   cbk::derotate_pack_kernel<<<blocks, 256, 0, st>>>(dp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "derotate_pack launch");
-  char* tables = static_cast<char*>(workspace) + ws_keys_bytes(m, n_tokens);
-  return launch_rope_table(st, dst_rope, position_start, n_tokens, reinterpret_cast<float*>(tables),
-                           reinterpret_cast<float*>(tables + ws_table_bytes(n_tokens)), n_tokens);
+  return CB_OK;
 }
 
 int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst,
-              int64_t n_tokens, const void* workspace, int32_t* dev_status) {
+              int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope, const void* workspace,
+              int32_t* dev_status) {
   cbk::MapTcParams p{};
   p.n_tokens = static_cast<int>(n_tokens);
   p.L_t = m->L_t;
@@ -173,19 +196,31 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
   if (items > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "work too large for one call");
   p.num_items = static_cast<int>(items);
-  p.w_resident = m->S <= 4;
+  // Weights stay resident for a whole item when they leave room for >= 2 A
+  // stages; otherwise two weight slots are streamed per m-tile.
+  const int res_stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(m->S, 0)) / cbk::kKBlockBytes;
+  p.w_resident = (m->S <= 4 && res_stages >= 2) ? 1 : 0;
   p.w_slots = p.w_resident ? m->S : 2;
   const int stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(p.w_slots, 0)) / cbk::kKBlockBytes;
   p.stages = std::min(stages, 4);
   if (p.stages < 2) return fail(CB_ERR_UNSUPPORTED, "shared memory too small for the pipeline");
   p.w_img = m->w_img;
-  p.bias = m->b32;
+  p.unit_bytes = static_cast<int64_t>(m->S) * cbk::kKBlockBytes + cbk::kBiasBlockBytes;
   p.sel_global = m->sel;
   p.sel_local = m->sel_local;
   p.ws_k = static_cast<const __nv_bfloat16*>(workspace);
   for (int l = 0; l < src->layers; ++l) p.src_v[l] = src->v[l];
   p.src_row_stride = src->row_stride;
   p.src_rows = src->rows;
+  {
+    const cuuint64_t kdims[4] = {128, static_cast<cuuint64_t>(m->H), static_cast<cuuint64_t>(n_tokens),
+                                 static_cast<cuuint64_t>(m->U)};
+    const cuuint64_t kstr[3] = {256, static_cast<cuuint64_t>(m->H) * 256,
+                                static_cast<cuuint64_t>(n_tokens) * m->H * 256};
+    const cuuint32_t kbox[4] = {64, 1, 128, 1};
+    int rc = encode_bf16_map(&p.kmap, 4, workspace, kdims, kstr, kbox);
+    if (rc != CB_OK) return rc;
+  }
   p.src_head_offset = src->head_offset;
   p.src_slot_dtype = src->slot_dtype;
   p.src_slots = src->slots;
@@ -198,9 +233,18 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.dst_head_offset = dst->head_offset;
   p.dst_slot_dtype = dst->slot_dtype;
   p.dst_slots = dst->slots;
-  const char* tables = static_cast<const char*>(workspace) + ws_keys_bytes(m, n_tokens);
-  p.dcos = reinterpret_cast<const float*>(tables);
-  p.dsin = reinterpret_cast<const float*>(tables + ws_table_bytes(n_tokens));
+  std::memcpy(p.dst_inv_freq, dst_rope->inv_freq, sizeof(p.dst_inv_freq));
+  p.dst_magnitude = dst_rope->magnitude;
+  p.position_start = position_start;
+  {
+    float max_inv = 0.f;
+    for (int i = 0; i < dst_rope->half_dim; ++i) max_inv = std::max(max_inv, std::fabs(dst_rope->inv_freq[i]));
+    p.trig_exact = static_cast<double>(position_start + n_tokens) * max_inv > 4.0e5 ? 1 : 0;
+  }
+  for (int k = 0; k < cbk::kTrigEntries; ++k) {
+    const double a = 6.283185307179586476925 * k / cbk::kTrigEntries;
+    p.trig[k] = make_float2(static_cast<float>(std::cos(a)), static_cast<float>(std::sin(a)));
+  }
   p.status = dev_status;
   const int smem = cbk::tc_smem_bytes(p.w_slots, p.stages);
   cudaError_t attr_err = cudaSuccess;
@@ -346,20 +390,26 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
   if ((e = cudaMemcpy(m->used_dev, m->used.data(), m->used.size() * sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload used");
 
   if (head_dim == cbk::kD) {
-    // Tensor-core image: for each (kind, layer, head, k-block j) a 32 KB block
+    // Tensor-core image, one unit per (kind, layer, head): S blocks of 32 KB
     // holding W^T (rows = output dim d, K-major = input feature) as two
-    // 128B-swizzled panels of 64 features; 16-byte chunk c of row d sits at
-    // chunk position c ^ (d & 7) of its 128-byte row.
+    // 128B-swizzled panels of 64 features (16-byte chunk c of row d at chunk
+    // position c ^ (d & 7) of its 128-byte row), then a 4 KB bias block: one
+    // K=16 step in no-swizzle K-major layout whose columns 0 and 1 hold
+    // bf16(bias) and bf16(bias - bf16(bias)), so ones @ block == bias to ~2^-17.
     const size_t units = 2ull * target_layers * heads;
-    std::vector<uint16_t> img(units * num_selected * (cbk::kKBlockBytes / 2));
+    const size_t unit_halfs = (static_cast<size_t>(num_selected) * cbk::kKBlockBytes + cbk::kBiasBlockBytes) / 2;
+    std::vector<uint16_t> img(units * unit_halfs, 0);
     for (int kind = 0; kind < 2; ++kind) {
       const float* W = kind ? v_weight : k_weight;
+      const float* B = kind ? v_bias : k_bias;
       for (int l = 0; l < target_layers; ++l)
         for (int h = 0; h < heads; ++h) {
           const float* wh = W + (static_cast<size_t>(l) * heads + h) * F * head_dim;
+          const float* bh = B + (static_cast<size_t>(l) * heads + h) * head_dim;
           const size_t unit = (static_cast<size_t>(kind) * target_layers + l) * heads + h;
+          uint16_t* base = img.data() + unit * unit_halfs;
           for (int j = 0; j < num_selected; ++j) {
-            uint16_t* blk = img.data() + (unit * num_selected + j) * (cbk::kKBlockBytes / 2);
+            uint16_t* blk = base + static_cast<size_t>(j) * (cbk::kKBlockBytes / 2);
             for (int f = 0; f < 128; ++f) {
               const int panel = f >> 6, chunk = (f & 63) >> 3, e8 = f & 7;
               const float* wrow = wh + static_cast<size_t>(j * 128 + f) * head_dim;
@@ -369,6 +419,17 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
                 blk[byte / 2] = f32_to_bf16_rne(wrow[d]);
               }
             }
+          }
+          uint16_t* bias_blk = base + static_cast<size_t>(num_selected) * (cbk::kKBlockBytes / 2);
+          for (int d = 0; d < 128; ++d) {
+            const uint16_t hi = f32_to_bf16_rne(bh[d]);
+            uint32_t hbits = static_cast<uint32_t>(hi) << 16;
+            float hf;
+            std::memcpy(&hf, &hbits, 4);
+            const uint16_t lo = f32_to_bf16_rne(bh[d] - hf);
+            const size_t b0 = (d / 8) * 256 + (d % 8) * 16;  // k = 0 and k = 1 of row d
+            bias_blk[b0 / 2] = hi;
+            bias_blk[b0 / 2 + 1] = lo;
           }
         }
     }
@@ -444,10 +505,9 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
 
   if (tc) {
     if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
-    if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, dst_rope, workspace, dev_status)) !=
-        CB_OK)
+    if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, workspace, dev_status)) != CB_OK)
       return rc;
-    return launch_tc(m, st, src, dst, n_tokens, workspace, dev_status);
+    return launch_tc(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, dev_status);
   }
 
   // Generic CUDA-core path.
@@ -491,31 +551,33 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
 }
 
 int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_tokens,
-                     int64_t position_start, const cb_rope* src_rope, const cb_rope* dst_rope,
-                     void* workspace, size_t workspace_bytes, int32_t* dev_status) {
+                     int64_t position_start, const cb_rope* src_rope, void* workspace,
+                     size_t workspace_bytes, int32_t* dev_status) {
   int rc = check_tc_call(m, src, nullptr, n_tokens);
   if (rc != CB_OK) return rc;
   if ((rc = check_rope(src_rope, m->D, "source RoPE")) != CB_OK) return rc;
+  if (position_start < 0) return fail(CB_ERR_INVALID, "negative position_start");
+  if (n_tokens == 0) return CB_OK;
+  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
+  DeviceGuard guard(m->device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, position_start, src_rope, workspace,
+                         dev_status);
+}
+
+int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
+                          int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope,
+                          const void* workspace, size_t workspace_bytes, int32_t* dev_status) {
+  int rc = check_tc_call(m, src, dst, n_tokens);
+  if (rc != CB_OK) return rc;
   if ((rc = check_rope(dst_rope, m->D, "target RoPE")) != CB_OK) return rc;
   if (position_start < 0) return fail(CB_ERR_INVALID, "negative position_start");
   if (n_tokens == 0) return CB_OK;
   if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
-  return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, position_start, src_rope, dst_rope,
-                         workspace, dev_status);
-}
-
-int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
-                          int64_t n_tokens, const void* workspace, size_t workspace_bytes,
-                          int32_t* dev_status) {
-  int rc = check_tc_call(m, src, dst, n_tokens);
-  if (rc != CB_OK) return rc;
-  if (n_tokens == 0) return CB_OK;
-  if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
-  DeviceGuard guard(m->device);
-  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
-  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, workspace, dev_status);
+  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, position_start, dst_rope, workspace,
+                   dev_status);
 }
 
 static int launch_copy_rows(cudaStream_t st, cbk::CopyRowsParams& p, int64_t n) {

@@ -5,6 +5,7 @@
 // parameter blocks every kernel receives by value.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -183,6 +184,42 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// TMA tiled load of a 4-D box into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// TMA gather of 4 rows (y0..y3, one-row box starting at column x) of a 2-D
+// tensor into 4 consecutive box rows of this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int y0, int y1, int y2,
+                                            int y3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
+      : "memory");
+}
+
+// L2 prefetches of the same boxes (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_gather4(const CUtensorMap* map, int x, int y0, int y1, int y2, int y3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+               : "memory");
 }
 
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {

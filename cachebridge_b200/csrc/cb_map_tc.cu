@@ -8,32 +8,39 @@
 // row straight into the target pool row dst_slots[t]
 // (online/blocks.py:86-111 set_kv_buffer; source_mapper_adapter.py:389-425).
 // Keys read the content-space (source-RoPE-removed, BF16-rounded) rows that
-// derotate_pack_kernel (cb_kernels.cu) packed into the workspace; values read the source pool rows
-// directly through src_slots (the gather of online/blocks.py:47-82).
+// derotate_pack_kernel (cb_kernels.cu) packed into the workspace; values read
+// the source pool rows directly through src_slots (the gather of
+// online/blocks.py:47-82).
 //
 // Work unit ("item"): (head h, kind, chunk of R*128 tokens, target layer l).
 // Items are ordered head/kind-major, then chunk, then layer, so the CTAs that
 // run concurrently share one head/kind's source rows of one token window
 // (each source row feeds ~L_t*S/L_s target layers and is read from HBM once)
-// and that head/kind's weights (L_t*S*32 KB) stay resident in L2.
+// and that head/kind's weights stay resident in L2.
 //
-// CTA (persistent, one per SM, 320 threads) roles:
-//   warps 0-3  producers: 16-byte cp.async gathers of 128 token rows x 256 B
-//              per k-block into a 128B-swizzled K-major stage (ring of NS).
-//   warps 4-11 epilogue, two groups of four warps that take alternate
-//              m-tiles; in a group, warp q reads TMEM lane quarter q (token
-//              rows 32q..32q+31, one row per thread). Per 32-pair half row:
-//              two tcgen05.ld rounds of 16 RoPE pairs (columns i and i+64),
-//              + bias, target RoPE (K), BF16, staging into the warp's
-//              swizzled 32 x 128 B tile, then 16-byte stores of 4 rows x
-//              (2 x 64 B) per warp instruction.
-//   warp 12    TMEM owner + single-thread tcgen05.mma issuer (M=128, N=128,
-//              K=16 steps; 8 steps per 128-feature k-block).
-//   warp 13    weight loader: one bulk copy per 32 KB weight k-block (the
-//              pre-swizzled image built at upload); resident for the whole
-//              item when S <= 4, streamed per m-tile otherwise.
-// Accumulators: 4 x (128 lanes x 128 fp32 columns) in TMEM (all 512 columns),
-// so the MMAs run up to three m-tiles ahead of the two epilogue groups.
+// CTA (persistent, one per SM, 576 threads) roles:
+//   warps 0-3   producers: per k-block one 32 KB stage (ring of NS) in the
+//               UMMA 128B-swizzled K-major layout: keys by two 4-D TMA tiled
+//               loads from the workspace, values by 16-byte cp.async gathers
+//               of the source pool rows through the slot table.
+//   warps 4-15  epilogue: three groups of four warps; group g takes the m-tiles
+//               n with n % 3 == g (TMEM accumulator n % 4). In a
+//               group, warp w reads TMEM lane quarter w % 4 (token rows, one
+//               per thread), in four rounds of 16 RoPE pairs (columns i and
+//               i+64): target RoPE for keys (coefficients from a table-driven
+//               sin/cos of the exact FP32 phase), BF16 packing, a swizzled
+//               32 x 64 B staging tile, then 16-byte stores of 8 rows x
+//               (2 x 32 B) per warp instruction.
+//   warp 16     TMEM owner + single-thread tcgen05.mma issuer: per m-tile one
+//               K=16 step that loads the bias (a constant ones column times a
+//               [bias_hi, bias_lo] block), then 8 K=16 steps per 128-feature
+//               k-block (M=128, N=128, BF16 in, FP32 accumulate).
+//   warp 17     weight loader: bulk copies of the unit's 4 KB bias block and
+//               its 32 KB W^T k-blocks (the pre-swizzled image built at
+//               upload); resident for the whole item when they fit, streamed
+//               per m-tile otherwise.
+// Every wait is bounded (kWaitTimeoutNs): an expired wait flags
+// CB_DEV_ERR_TIMEOUT and the CTA unwinds instead of hanging.
 #include "cb_device.cuh"
 #include "cb_map_tc.cuh"
 
@@ -45,9 +52,11 @@ constexpr int kBarFull = 0;       // [4]  producers -> MMA (A stage filled)
 constexpr int kBarEmpty = 4;      // [4]  MMA -> producers (A stage consumed)
 constexpr int kBarWFull = 8;      // [4]  loader -> MMA (weight slot filled)
 constexpr int kBarWEmpty = 12;    // [4]  MMA -> loader (weight slot consumed)
-constexpr int kBarAccFull = 16;   // [4]  MMA -> epilogue (accumulator ready)
-constexpr int kBarAccEmpty = 20;  // [4]  epilogue -> MMA (accumulator drained)
-constexpr int kBarDone = 24;      // [1]  MMA drain at exit
+constexpr int kBarAccFull = 16;   // [4]  MMA -> epilogue group (accumulator ready)
+constexpr int kBarAccEmpty = 20;  // [4]  epilogue group -> MMA (accumulator drained)
+constexpr int kBarBFull = 24;     // [1]  loader -> MMA (bias block filled)
+constexpr int kBarBEmpty = 25;    // [1]  MMA -> loader (bias block consumed)
+constexpr int kBarDone = 26;      // [1]  MMA drain at exit
 constexpr int kNumBars = 32;
 
 struct Item {
@@ -75,38 +84,80 @@ __device__ __forceinline__ Item decode_item(const MapTcParams& p, int i) {
 }
 
 struct Smem {
-  uint32_t w;     // weight slots base (shared::cta address)
-  uint32_t a;     // A stages base
-  uint32_t e;     // epilogue staging base
-  uint8_t* e_gen; // generic pointer to epilogue staging
-  uint32_t bars;  // mbarrier array base
+  uint32_t w;      // weight slots (shared::cta address)
+  uint32_t bias;   // bias block slot
+  uint32_t a;      // A stages
+  uint32_t ones;   // constant ones block
+  uint8_t* e_gen;  // epilogue staging (generic pointer)
+  const float2* trig;
+  uint32_t bars;   // mbarrier array
   uint32_t* tmem_holder;
   volatile int* abort_flag;
 };
 
 __device__ __forceinline__ uint32_t bar_at(const Smem& s, int idx) { return s.bars + 8u * idx; }
 
+// UMMA descriptor of one K=16 step of a 128-row K-major operand without
+// swizzle: 8-row x 16-byte core matrices, the two K halves 128 B apart
+// (leading byte offset), consecutive 8-row groups 256 B apart (stride byte
+// offset). Element (row r, k) sits at (r/8)*256 + (k/8)*128 + (r%8)*16 + (k%8)*2.
+__device__ __forceinline__ uint64_t make_noswizzle_k16_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(128u >> 4) << 16;
+  d |= static_cast<uint64_t>(256u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  return d;  // layout type 0: no swizzle
+}
+
+// Table-driven sin/cos of an FP32 phase (Tang's method): phi = k*(2pi/128) + r
+// by a two-constant Cody-Waite reduction with FMA, |r| <= pi/128 (+ rounding
+// slack), (cos, sin)(2pi k/128) from a 128-entry table, cos(r) and sin(r) from
+// their Taylor series (truncation below 1e-12 for |r| < 0.05). The result is
+// within a few FP32 ulps of cos/sin(phi) for |phi| < 4e5 (k stays an exact
+// FP32 integer); calls with larger phases use sincosf (MapTcParams::trig_exact).
+__device__ __forceinline__ void sincos_tab(float phi, const float2* tab, float& c, float& s) {
+  const float kInvStep = 0x1.45f306p+4f;    // 128 / (2 pi)
+  const float kStepHi = 0x1.921fb6p-5f;     // fl(2 pi / 128)
+  const float kStepLo = -0x1.777a5cp-30f;   // 2 pi / 128 - kStepHi
+  const float kf = rintf(phi * kInvStep);
+  float r = fmaf(-kf, kStepHi, phi);
+  r = fmaf(-kf, kStepLo, r);
+  const float2 cs = tab[static_cast<int>(kf) & (kTrigEntries - 1)];
+  const float r2 = r * r;
+  const float sr = fmaf(r * r2, fmaf(r2, 1.0f / 120.0f, -1.0f / 6.0f), r);
+  const float cr = fmaf(r2, fmaf(r2, 1.0f / 24.0f, -0.5f), 1.0f);
+  c = fmaf(cs.x, cr, -cs.y * sr);
+  s = fmaf(cs.y, cr, cs.x * sr);
+}
+
 // ------------------------------- producers ---------------------------------
+// Four warps; warp pw owns token rows [32 pw, 32 pw + 32) of every stage.
+// Keys: thread 0 loads the stage with two 4-D TMA boxes (128 tokens x 64
+// features) from the content-space workspace (expect_tx 32 KB). Values:
+// 16-byte cp.async gathers of the source pool rows through the slot table,
+// 16 lanes per 256-byte row, two rows per warp instruction, tracked by
+// cp.async.mbarrier.arrive.noinc. The stage's full barrier counts 129
+// arrivals: one per producer thread plus thread 0's expect_tx.
 __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int lane) {
   const int NS = p.stages;
+  const bool leader = pw == 0 && lane == 0;
   int issued = 0;
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    // Slot of this lane's token row, prefetched one m-tile ahead.
-    const int lane_row = pw * 32 + lane;
-    int next_t = it.tok0 + lane_row;
+    // Slot of this lane's token row, prefetched one m-tile ahead (values only).
+    int next_t = it.tok0 + pw * 32 + lane;
     int next_valid = next_t < p.n_tokens;
-    int64_t next_row = next_t;
-    if (it.kind == 1 && next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, next_t);
+    int64_t next_row = next_valid && it.kind == 1 ? load_slot(p.src_slots, p.src_slot_dtype, next_t) : 0;
     for (int m = 0; m < it.mtiles && ok; ++m) {
+      const int tok0 = it.tok0 + m * kBM;
       int valid = next_valid;
       int64_t srow = next_row;
       if (m + 1 < it.mtiles) {
         next_t += kBM;
         next_valid = next_t < p.n_tokens;
-        next_row = next_t;
-        if (it.kind == 1 && next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, next_t);
+        next_row = next_valid && it.kind == 1 ? load_slot(p.src_slots, p.src_slot_dtype, next_t) : 0;
       }
       if (it.kind == 1 && valid && (srow < 0 || srow >= p.src_rows)) {
         flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
@@ -115,41 +166,40 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
       for (int j = 0; j < p.S; ++j) {
         const int stage = issued % NS;
         // Warp-uniform outcome: the gather below uses full-warp shuffles.
-        const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), ((issued / NS) & 1) ^ 1,
-                                   s.abort_flag, p.status);
+        const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), ((issued / NS) & 1) ^ 1, s.abort_flag, p.status);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        const char* base;
-        int64_t stride_bytes;
+        const uint32_t full = bar_at(s, kBarFull + stage);
+        const uint32_t dst = s.a + stage * kKBlockBytes;
         if (it.kind == 0) {
-          const int u = __ldg(p.sel_local + it.l * p.S + j);
-          base = reinterpret_cast<const char*>(p.ws_k) +
-                 ((static_cast<int64_t>(u) * p.n_tokens) * p.H + it.h) * (kD * 2);
-          stride_bytes = static_cast<int64_t>(p.H) * kD * 2;
+          if (leader) {
+            const int u = __ldg(p.sel_local + it.l * p.S + j);
+            mbar_arrive_expect_tx(full, kKBlockBytes);
+            tma_load_4d(dst, &p.kmap, 0, it.h, tok0, u, full);
+            tma_load_4d(dst + kPanelBytes, &p.kmap, 64, it.h, tok0, u, full);
+          }
+          mbar_arrive(full);
         } else {
           const int sl = __ldg(p.sel_global + it.l * p.S + j);
-          base = reinterpret_cast<const char*>(p.src_v[sl]) +
-                 static_cast<int64_t>(p.src_head_offset + it.h) * (kD * 2);
-          stride_bytes = p.src_row_stride * 2;
-        }
-        const uint32_t stage_addr = s.a + stage * kKBlockBytes;
-        const int c = lane & 15;
+          const char* base = reinterpret_cast<const char*>(p.src_v[sl]) +
+                             static_cast<int64_t>(p.src_head_offset + it.h) * (kD * 2);
+          const int64_t stride_bytes = p.src_row_stride * 2;
+          const int c = lane & 15;
 #pragma unroll
-        for (int ii = 0; ii < 16; ++ii) {
-          const int r = 2 * ii + (lane >> 4);
-          const int64_t rr = __shfl_sync(0xffffffffu, srow, r);
-          const int vv = __shfl_sync(0xffffffffu, valid, r);
-          const int row = pw * 32 + r;
-          const char* g = base + (vv ? rr * stride_bytes : 0) + c * 16;
-          const uint32_t dst =
-              stage_addr + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-          cp_async_16(dst, g, vv ? 16u : 0u);
+          for (int ii = 0; ii < 16; ++ii) {
+            const int r = 2 * ii + (lane >> 4);
+            const int64_t rr = __shfl_sync(0xffffffffu, srow, r);
+            const int vv = __shfl_sync(0xffffffffu, valid, r);
+            const int row = pw * 32 + r;
+            const char* g = base + (vv ? rr * stride_bytes : 0) + c * 16;
+            const uint32_t d = dst + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+            cp_async_16(d, g, vv ? 16u : 0u);
+          }
+          cp_async_arrive_noinc(full);
+          if (leader) mbar_arrive(full);
         }
-        // The stage's full barrier (count 128) completes when every producer
-        // thread's copies have landed, independently of the producer's progress.
-        cp_async_arrive_noinc(bar_at(s, kBarFull + stage));
         ++issued;
       }
     }
@@ -163,13 +213,17 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
   const uint64_t policy = l2_policy_evict_last();
   int wq = 0, itc = 0;
   bool ok = true;
-  // Track the last load issued into each slot so an aborted CTA can wait for
-  // its own bulk copies before exiting.
-  int last_par[4] = {-1, -1, -1, -1};
+  // The last load issued into each weight slot (and the bias slot, index 4),
+  // so an aborted CTA can wait for its own bulk copies before exiting.
+  int last_par[5] = {-1, -1, -1, -1, -1};
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    const uint8_t* wu =
-        p.w_img + (static_cast<int64_t>((it.kind * p.L_t + it.l) * p.H + it.h) * p.S) * kKBlockBytes;
+    const uint8_t* wu = p.w_img + static_cast<int64_t>((it.kind * p.L_t + it.l) * p.H + it.h) * p.unit_bytes;
+    if (!mbar_wait(bar_at(s, kBarBEmpty), (itc & 1) ^ 1, s.abort_flag, p.status)) break;
+    mbar_arrive_expect_tx(bar_at(s, kBarBFull), kBiasBlockBytes);
+    bulk_copy_g2s(s.bias, wu + static_cast<int64_t>(p.S) * kKBlockBytes, kBiasBlockBytes, bar_at(s, kBarBFull),
+                  policy);
+    last_par[4] = itc & 1;
     if (p.w_resident) {
       for (int j = 0; j < p.S; ++j) {
         if (!mbar_wait(bar_at(s, kBarWEmpty + j), (itc & 1) ^ 1, s.abort_flag, p.status)) {
@@ -177,22 +231,21 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
           break;
         }
         mbar_arrive_expect_tx(bar_at(s, kBarWFull + j), kKBlockBytes);
-        bulk_copy_g2s(s.w + j * kKBlockBytes, wu + static_cast<int64_t>(j) * kKBlockBytes,
-                      kKBlockBytes, bar_at(s, kBarWFull + j), policy);
+        bulk_copy_g2s(s.w + j * kKBlockBytes, wu + static_cast<int64_t>(j) * kKBlockBytes, kKBlockBytes,
+                      bar_at(s, kBarWFull + j), policy);
         last_par[j] = itc & 1;
       }
     } else {
       for (int m = 0; m < it.mtiles && ok; ++m) {
         for (int j = 0; j < p.S; ++j) {
           const int slot = wq & 1;
-          if (!mbar_wait(bar_at(s, kBarWEmpty + slot), ((wq >> 1) & 1) ^ 1, s.abort_flag,
-                         p.status)) {
+          if (!mbar_wait(bar_at(s, kBarWEmpty + slot), ((wq >> 1) & 1) ^ 1, s.abort_flag, p.status)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(bar_at(s, kBarWFull + slot), kKBlockBytes);
-          bulk_copy_g2s(s.w + slot * kKBlockBytes, wu + static_cast<int64_t>(j) * kKBlockBytes,
-                        kKBlockBytes, bar_at(s, kBarWFull + slot), policy);
+          bulk_copy_g2s(s.w + slot * kKBlockBytes, wu + static_cast<int64_t>(j) * kKBlockBytes, kKBlockBytes,
+                        bar_at(s, kBarWFull + slot), policy);
           last_par[slot] = (wq >> 1) & 1;
           ++wq;
         }
@@ -200,12 +253,13 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
     }
     ++itc;
   }
-  if (!ok) {
+  if (*s.abort_flag) {
     // Aborted: wait (bounded) for this thread's own copies still in flight.
     const uint64_t t0 = global_timer_ns();
-    for (int slot = 0; slot < 4; ++slot) {
-      if (last_par[slot] < 0) continue;
-      while (!mbar_try_wait(bar_at(s, kBarWFull + slot), last_par[slot])) {
+    for (int k = 0; k < 5; ++k) {
+      if (last_par[k] < 0) continue;
+      const uint32_t bar = k < 4 ? bar_at(s, kBarWFull + k) : bar_at(s, kBarBFull);
+      while (!mbar_try_wait(bar, last_par[k])) {
         if (global_timer_ns() - t0 > kWaitTimeoutNs) break;
       }
     }
@@ -215,29 +269,31 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
 // ------------------------------- MMA issuer --------------------------------
 __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base) {
   constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, kD);
+  const uint64_t ones_desc = make_noswizzle_k16_desc(s.ones);
+  const uint64_t bias_desc = make_noswizzle_k16_desc(s.bias);
   const int NS = p.stages;
-  int q = 0, wq = 0, accc = 0, itc = 0;
+  int q = 0, wq = 0, n = 0, itc = 0;
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    for (int m = 0; m < it.mtiles && ok; ++m) {
-      const int acc = accc & 3;
-      if (!mbar_wait(bar_at(s, kBarAccEmpty + acc), ((accc >> 2) & 1) ^ 1, s.abort_flag,
-                     p.status)) {
+    if (!mbar_wait(bar_at(s, kBarBFull), itc & 1, s.abort_flag, p.status)) break;
+    for (int m = 0; m < it.mtiles && ok; ++m, ++n) {
+      const int acc = n & 3;
+      if (!mbar_wait(bar_at(s, kBarAccEmpty + acc), ((n >> 2) & 1) ^ 1, s.abort_flag, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * kD;
+      // Accumulator := ones[:, 0:2] @ [bias_hi; bias_lo] = bias (FP32).
+      umma_bf16(d_tmem, ones_desc, bias_desc, idesc, 0u);
       for (int j = 0; j < p.S; ++j) {
         int wslot;
         if (p.w_resident) {
           wslot = j;
-          if (m == 0) {
-            if (!mbar_wait(bar_at(s, kBarWFull + j), itc & 1, s.abort_flag, p.status)) {
-              ok = false;
-              break;
-            }
+          if (m == 0 && !mbar_wait(bar_at(s, kBarWFull + j), itc & 1, s.abort_flag, p.status)) {
+            ok = false;
+            break;
           }
         } else {
           wslot = wq & 1;
@@ -252,13 +308,15 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
           break;
         }
         tc_fence_after();
+        // Value stages were written by cp.async (generic proxy); the MMA reads
+        // them through the async proxy.
+        if (it.kind == 1) fence_proxy_async_smem();
         const uint32_t a0 = s.a + stage * kKBlockBytes;
         const uint32_t b0 = s.w + wslot * kKBlockBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kPanelBytes + (kk & 3) * 32;
-          umma_bf16(d_tmem, make_sw128_kmajor_desc(a0 + off), make_sw128_kmajor_desc(b0 + off),
-                    idesc, (j | kk) != 0 ? 1u : 0u);
+          umma_bf16(d_tmem, make_sw128_kmajor_desc(a0 + off), make_sw128_kmajor_desc(b0 + off), idesc, 1u);
         }
         umma_commit(bar_at(s, kBarEmpty + stage));
         if (!p.w_resident) {
@@ -269,10 +327,11 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
       }
       if (!ok) break;
       umma_commit(bar_at(s, kBarAccFull + acc));
-      ++accc;
     }
-    if (ok && p.w_resident) {
-      for (int j = 0; j < p.S; ++j) umma_commit(bar_at(s, kBarWEmpty + j));
+    if (ok) {
+      umma_commit(bar_at(s, kBarBEmpty));
+      if (p.w_resident)
+        for (int j = 0; j < p.S; ++j) umma_commit(bar_at(s, kBarWEmpty + j));
     }
     ++itc;
   }
@@ -288,141 +347,104 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
 }
 
 // -------------------------------- epilogue ---------------------------------
-__device__ __forceinline__ void load16(const float* src, float (&out)[16]) {
-  const float4* v = reinterpret_cast<const float4*>(src);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 x = __ldg(v + q);
-    out[4 * q + 0] = x.x;
-    out[4 * q + 1] = x.y;
-    out[4 * q + 2] = x.z;
-    out[4 * q + 3] = x.w;
-  }
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 r;
+  r.x = pack_bf16x2(v[0], v[1]);
+  r.y = pack_bf16x2(v[2], v[3]);
+  r.z = pack_bf16x2(v[4], v[5]);
+  r.w = pack_bf16x2(v[6], v[7]);
+  return r;
 }
 
-// Warp (group g, quarter eq): m-tiles n with n % 2 == g, token rows eq*32 + lane.
-// Target RoPE coefficients come from the frequency-major table [64][n] that
-// phase 1 wrote: one load instruction fetches one frequency for the warp's 32
-// consecutive tokens (one 128-byte line); the next round's 16 are fetched while
-// the current round computes.
-__device__ __forceinline__ void load_rope16(const float* cos_row0, const float* sin_row0, int64_t rs,
-                                            float (&c)[16], float (&s)[16]) {
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    c[e] = __ldg(cos_row0 + e * rs);
-    s[e] = __ldg(sin_row0 + e * rs);
-  }
-}
-
-__device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int g, int eq,
-                             int lane) {
-  uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 128 B, this warp only
-  uint8_t* my_row = stage + lane * 128;
+// Warp (group g, lane quarter eq): the m-tiles n with n % 4 == g, token rows
+// eq*32 + lane (one per thread), accumulator g.
+__device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int g, int eq, int lane) {
+  uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 64 B, this warp only
+  uint8_t* my_row = stage + lane * 64;
+  const int my_key = (lane >> 1) & 3;  // staging swizzle of this lane's row
   const int64_t dst_stride_bytes = p.dst_row_stride * 2;
-  const int64_t rs = p.n_tokens;
-  int accc = 0;  // CTA-wide m-tile counter (both groups count every m-tile)
+  const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eq * 32) << 16);
+  int n = 0;  // CTA m-tile counter
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    const float* bias = p.bias + (static_cast<int64_t>(it.kind * p.L_t + it.l) * p.H + it.h) * kD;
     char* dst_layer = reinterpret_cast<char*>(it.kind ? p.dst_v[it.l] : p.dst_k[it.l]) +
                       static_cast<int64_t>(p.dst_head_offset + it.h) * (kD * 2);
-    for (int m = 0; m < it.mtiles; ++m, ++accc) {
-      if ((accc & 1) != g) continue;
+    for (int m = 0; m < it.mtiles; ++m, ++n) {
+      if (n % kEpiGroups != g) continue;
+      const int acc = n & 3;  // accumulator buffer of this m-tile
+      const uint32_t tbase = lane_base + acc * kD;
       const int t = it.tok0 + m * kBM + eq * 32 + lane;
-      int valid = t < p.n_tokens;
-      int64_t dslot = valid ? load_slot(p.dst_slots, p.dst_slot_dtype, t) : 0;
-      if (valid && (dslot < 0 || dslot >= p.dst_rows)) {
-        flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-        valid = 0;
+      char* row_ptr = nullptr;  // this lane's destination row, or null
+      if (t < p.n_tokens) {
+        const int64_t slot = load_slot(p.dst_slots, p.dst_slot_dtype, t);
+        if (slot < 0 || slot >= p.dst_rows)
+          flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+        else
+          row_ptr = dst_layer + slot * dst_stride_bytes;
       }
-      const bool do_rope = it.kind == 0 && valid;
-      const float* cbase = p.dcos + t;
-      const float* sbase = p.dsin + t;
-      float ca[16], sa[16];  // coefficients of the current 16-pair round
-      if (do_rope) load_rope16(cbase, sbase, rs, ca, sa);
-      const int acc = accc & 3;
+      const bool do_rope = it.kind == 0 && row_ptr != nullptr;
+      const float pos = static_cast<float>(p.position_start + t);
       // Warp-uniform outcome: tcgen05.ld is .sync.aligned across the warp.
-      const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (accc >> 2) & 1, s.abort_flag, p.status);
+      const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (n >> 2) & 1, s.abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(eq * 32) << 16) + acc * kD;
+#pragma unroll 1
+      for (int r = 0; r < 4; ++r) {  // RoPE pairs [16r, 16r + 16)
+        const int p0 = 16 * r;
+        uint32_t lo[16], hi[16];
+        tmem_ld_32x32b_x16(tbase + p0, lo);
+        tmem_ld_32x32b_x16(tbase + 64 + p0, hi);
+        tmem_wait_ld();
+        if (r == 3) {
+          // Accumulator fully read into registers: hand it back to the MMA.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
+        }
+        float ylo[16], yhi[16];
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {  // RoPE pairs [32hb, 32hb+32)
-#pragma unroll
-        for (int sr = 0; sr < 2; ++sr) {  // 16-pair round
-          const int p0 = 32 * hb + 16 * sr;  // first pair of the round
-          uint32_t lo[16], hi[16];
-          tmem_ld_32x32b_x16(tbase + p0, lo);
-          tmem_ld_32x32b_x16(tbase + 64 + p0, hi);
-          float cb[16], sb[16];  // next round's coefficients, fetched while this one computes
-          const bool prefetch = do_rope && p0 + 16 < 64;
-          if (prefetch) load_rope16(cbase + (p0 + 16) * rs, sbase + (p0 + 16) * rs, rs, cb, sb);
-          tmem_wait_ld();
-          if (hb == 1 && sr == 1) {
-            // Accumulator fully read into registers: hand it back to the MMA.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
+        for (int e = 0; e < 16; ++e) {
+          ylo[e] = __uint_as_float(lo[e]);
+          yhi[e] = __uint_as_float(hi[e]);
+        }
+        if (do_rope && p.trig_exact) {
+          for (int e = 0; e < 16; ++e) {
+            float c, sn, o0, o1;
+            sincosf(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), &sn, &c);
+            rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
+            ylo[e] = o0;
+            yhi[e] = o1;
           }
-          float blo[16], bhi[16];
-          load16(bias + p0, blo);
-          load16(bias + 64 + p0, bhi);
-          float ylo[16], yhi[16];
+        } else if (do_rope) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            ylo[e] = __fadd_rn(__uint_as_float(lo[e]), blo[e]);
-            yhi[e] = __fadd_rn(__uint_as_float(hi[e]), bhi[e]);
-          }
-          if (do_rope) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              float o0, o1;
-              rope_apply_pair(ylo[e], yhi[e], ca[e], sa[e], o0, o1);
-              ylo[e] = o0;
-              yhi[e] = o1;
-            }
-          }
-          if (prefetch) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              ca[e] = cb[e];
-              sa[e] = sb[e];
-            }
-          }
-          // Local chunk lc of the warp's 128-byte row piece: 0-3 = columns
-          // [32hb, 32hb+32), 4-7 = [64+32hb, ...); it sits at lc ^ (row & 7).
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            uint4 vlo, vhi;
-            vlo.x = pack_bf16x2(ylo[8 * k + 0], ylo[8 * k + 1]);
-            vlo.y = pack_bf16x2(ylo[8 * k + 2], ylo[8 * k + 3]);
-            vlo.z = pack_bf16x2(ylo[8 * k + 4], ylo[8 * k + 5]);
-            vlo.w = pack_bf16x2(ylo[8 * k + 6], ylo[8 * k + 7]);
-            vhi.x = pack_bf16x2(yhi[8 * k + 0], yhi[8 * k + 1]);
-            vhi.y = pack_bf16x2(yhi[8 * k + 2], yhi[8 * k + 3]);
-            vhi.z = pack_bf16x2(yhi[8 * k + 4], yhi[8 * k + 5]);
-            vhi.w = pack_bf16x2(yhi[8 * k + 6], yhi[8 * k + 7]);
-            const int llo = 2 * sr + k;
-            const int lhi = 4 + 2 * sr + k;
-            *reinterpret_cast<uint4*>(my_row + ((llo ^ (lane & 7)) << 4)) = vlo;
-            *reinterpret_cast<uint4*>(my_row + ((lhi ^ (lane & 7)) << 4)) = vhi;
+            float c, sn, o0, o1;
+            sincos_tab(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), s.trig, c, sn);
+            rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
+            ylo[e] = o0;
+            yhi[e] = o1;
           }
         }
+        // Local chunk lc of the round's 64-byte row piece (0-1: columns
+        // [p0, p0+16), 2-3: [64+p0, ...)) sits at lc ^ ((row >> 1) & 3).
+        *reinterpret_cast<uint4*>(my_row + ((0 ^ my_key) << 4)) = pack8(ylo);
+        *reinterpret_cast<uint4*>(my_row + ((1 ^ my_key) << 4)) = pack8(ylo + 8);
+        *reinterpret_cast<uint4*>(my_row + ((2 ^ my_key) << 4)) = pack8(yhi);
+        *reinterpret_cast<uint4*>(my_row + ((3 ^ my_key) << 4)) = pack8(yhi + 8);
         __syncwarp();
-        // Stores: 4 rows x (2 x 64 contiguous bytes) per warp instruction.
-        const int lc = lane & 7;
-        const int gchunk = lc < 4 ? 4 * hb + lc : 8 + 4 * hb + (lc - 4);
+        // Stores: 8 rows x (2 x 32 contiguous bytes) per warp instruction.
+        const int lc = lane & 3;
+        const int gchunk = lc < 2 ? 2 * r + lc : 8 + 2 * r + (lc - 2);
 #pragma unroll
-        for (int ii = 0; ii < 8; ++ii) {
-          const int rr = 4 * ii + (lane >> 3);
-          const int64_t sl = __shfl_sync(0xffffffffu, dslot, rr);
-          const int vv = __shfl_sync(0xffffffffu, valid, rr);
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((lc ^ (rr & 7)) << 4));
-          if (vv) *reinterpret_cast<uint4*>(dst_layer + sl * dst_stride_bytes + gchunk * 16) = v;
+        for (int qq = 0; qq < 4; ++qq) {
+          const int rr = 8 * qq + (lane >> 2);
+          char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((lc ^ ((rr >> 1) & 3)) << 4));
+          if (dst != nullptr) *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
         }
         __syncwarp();
       }
@@ -441,10 +463,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
 
   Smem s;
   s.w = base;
-  s.a = base + p.w_slots * kKBlockBytes;
-  s.e = s.a + p.stages * kKBlockBytes;
-  s.e_gen = base_gen + (s.e - base);
-  s.bars = s.e + kEpiWarps * kEpiWarpBytes;
+  s.a = s.w + p.w_slots * kKBlockBytes;
+  s.bias = s.a + p.stages * kKBlockBytes;
+  s.ones = s.bias + kBiasBlockBytes;
+  const uint32_t e = s.ones + kOnesBytes;
+  s.e_gen = base_gen + (e - base);
+  const uint32_t trig = e + kEpiWarps * kEpiWarpBytes;
+  float2* trig_gen = reinterpret_cast<float2*>(base_gen + (trig - base));
+  s.trig = trig_gen;
+  s.bars = trig + kTrigEntries * 8;
   uint8_t* bars_gen = base_gen + (s.bars - base);
   s.tmem_holder = reinterpret_cast<uint32_t*>(bars_gen + 8 * kNumBars);
   s.abort_flag = reinterpret_cast<volatile int*>(bars_gen + 8 * kNumBars + 4);
@@ -454,24 +481,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
-      mbar_init(bar_at(s, kBarFull + i), 128);
+      mbar_init(bar_at(s, kBarFull + i), 32 * kProdWarps + 1);  // producer threads + expect_tx
       mbar_init(bar_at(s, kBarEmpty + i), 1);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(bar_at(s, kBarWFull + i), 1);
       mbar_init(bar_at(s, kBarWEmpty + i), 1);
-    }
-    for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(bar_at(s, kBarAccFull + i), 1);
-      mbar_init(bar_at(s, kBarAccEmpty + i), 4);  // the 4 warps of the group that owns the m-tile
+      mbar_init(bar_at(s, kBarAccEmpty + i), 4);  // the 4 warps of the group owning the accumulator
     }
+    mbar_init(bar_at(s, kBarBFull), 1);
+    mbar_init(bar_at(s, kBarBEmpty), 1);
     mbar_init(bar_at(s, kBarDone), 1);
     *s.abort_flag = 0;
     fence_mbarrier_init();
+  }
+  // Constant operands: the ones block (rows of [1, 1, 0 x 14], no-swizzle
+  // K-major layout) and the (cos, sin) table.
+  {
+    uint16_t* ones = reinterpret_cast<uint16_t*>(base_gen + (s.ones - base));
+    for (int idx = threadIdx.x; idx < kOnesBytes / 2; idx += blockDim.x) {
+      const int kidx = ((idx >> 6) & 1) * 8 + (idx & 7);  // (byte/128 % 2) * 8 + byte%16/2
+      ones[idx] = kidx < 2 ? static_cast<uint16_t>(0x3F80) : static_cast<uint16_t>(0);
+    }
+    for (int idx = threadIdx.x; idx < kTrigEntries; idx += blockDim.x) trig_gen[idx] = p.trig[idx];
     fence_proxy_async_smem();
   }
-  constexpr int kMmaWarp = 4 + kEpiWarps;
-  constexpr int kLoaderWarp = kMmaWarp + 1;
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(s.tmem_holder), kTmemCols);
     tmem_relinquish();
@@ -481,15 +516,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_holder;
 
-  if (warp < 4) {
+  if (warp < kProdWarps) {
     run_producer(p, s, warp, lane);
   } else if (warp < kMmaWarp) {
-    // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule); group = (warp - 4) / 4.
-    run_epilogue(p, s, tmem_base, (warp - 4) >> 2, warp & 3, lane);
+    // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule).
+    run_epilogue(p, s, tmem_base, (warp - kProdWarps) >> 2, warp & 3, lane);
   } else if (warp == kMmaWarp) {
     if (lane == 0) run_mma(p, s, tmem_base);
     __syncwarp();
-  } else if (warp == kLoaderWarp) {
+  } else {
     if (lane == 0) run_weight_loader(p, s);
     __syncwarp();
   }

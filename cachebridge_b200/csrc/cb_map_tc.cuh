@@ -11,11 +11,18 @@ constexpr int kD = 128;                        // head_dim of the tensor-core pa
 constexpr int kBM = 128;                       // tokens per m-tile (UMMA M)
 constexpr int kPanelBytes = 128 * 128;         // 128 rows x 64 bf16 (one 128B-swizzle panel)
 constexpr int kKBlockBytes = 2 * kPanelBytes;  // 128 rows x 128 bf16: one source layer's head
-constexpr int kEpiWarps = 8;                   // two groups of 4 (one warp per TMEM lane quarter)
-constexpr int kEpiWarpBytes = 32 * 128;        // 32 token rows x 128 B staging per epilogue warp
+constexpr int kBiasBlockBytes = 128 * 32;      // one K=16 step x 128 rows (no swizzle): bias rows
+constexpr int kOnesBytes = 128 * 32;           // one K=16 step x 128 rows: constant 1.0 columns
+constexpr int kProdWarps = 4;                  // producer warps (cp.async value gathers, TMA keys)
+constexpr int kEpiGroups = 3;                  // epilogue groups (one m-tile each in flight)
+constexpr int kEpiWarps = 4 * kEpiGroups;      // one warp per TMEM lane quarter per group
+constexpr int kMmaWarp = kProdWarps + kEpiWarps;
+constexpr int kLoaderWarp = kMmaWarp + 1;
+constexpr int kTcThreads = 32 * (kLoaderWarp + 1);
 constexpr int kAccBufs = 4;                    // FP32 accumulators in TMEM (128 columns each)
-constexpr int kTcThreads = 32 * (4 + kEpiWarps + 2);  // producers, epilogue, MMA, loader
 constexpr int kTmemCols = 128 * kAccBufs;      // all 512 TMEM columns
+constexpr int kEpiWarpBytes = 32 * 64;         // 32 token rows x 64 B staging per epilogue warp
+constexpr int kTrigEntries = 128;              // (cos, sin)(2*pi*k/128) table
 constexpr int kTcMaxSmem = 232448;             // sm_100 opt-in dynamic shared memory per block
 
 struct MapTcParams {
@@ -30,8 +37,8 @@ struct MapTcParams {
   int stages;    // A stages (ring)
   int w_resident;
 
-  const uint8_t* w_img;     // [2 kinds][L_t][H][S][32 KB] pre-swizzled bf16 W^T k-blocks
-  const float* bias;        // [2 kinds][L_t][H][128] fp32
+  const uint8_t* w_img;     // per unit: S x 32 KB W^T k-blocks (128B-swizzled) + 4 KB bias block
+  int64_t unit_bytes;       // S * 32 KB + 4 KB
   const int* sel_global;    // [L_t][S] source layer ids
   const int* sel_local;     // [L_t][S] index into the workspace's used-layer list
 
@@ -51,17 +58,26 @@ struct MapTcParams {
   int dst_slot_dtype;
   const void* dst_slots;
 
-  const float* dcos;  // [64][n_tokens] target RoPE coefficients (workspace tail)
-  const float* dsin;
+  float dst_inv_freq[64];   // target RoPE
+  float dst_magnitude;
+  int64_t position_start;   // absolute position of token 0
+  int trig_exact;           // 1 when a phase can exceed the table method's range: use sincosf
+  float2 trig[kTrigEntries];  // (cos, sin)(2*pi*k/128), rounded to FP32 from double
   int32_t* status;
+  // 4-D map of the key workspace {128, H, n_tokens, U}, box {64, 1, 128, 1},
+  // 128B-swizzled, so a box lands in the UMMA K-major SW128 layout.
+  CUtensorMap kmap;
 };
 
 __global__ void map_install_tc_kernel(const __grid_constant__ MapTcParams p);
 
+// Shared memory bytes of everything but the weight slots and A stages.
+constexpr int kTcFixedSmem = 1024 /* alignment slack */ + kBiasBlockBytes + kOnesBytes +
+                             kEpiWarps * kEpiWarpBytes + kTrigEntries * 8 + 512 /* barriers */;
+
 // Shared-memory bytes the kernel needs for a given weight-slot / stage split.
 inline int tc_smem_bytes(int w_slots, int stages) {
-  return 1024 /* alignment slack */ + (w_slots + stages) * kKBlockBytes + kEpiWarps * kEpiWarpBytes +
-         512 /* barriers, TMEM holder, abort flag */;
+  return kTcFixedSmem + (w_slots + stages) * kKBlockBytes;
 }
 
 }  // namespace cbk

@@ -342,12 +342,12 @@ class HandoffCall:
 
     def derotate(self) -> None:
         """Phase 1 of the tensor-core path (``cb_derotate_keys``): content-space
-        keys and the target RoPE coefficients into the workspace."""
+        keys into the workspace."""
         nat.check(
             nat.load().cb_derotate_keys(
                 self.mapper._handle, self._stream(), ctypes.byref(self.src_c), self.n, self.position_start,
-                ctypes.byref(self.src_rope), ctypes.byref(self.dst_rope), self.workspace.data_ptr(),
-                self.workspace.numel(), self.status.data_ptr(),
+                ctypes.byref(self.src_rope), self.workspace.data_ptr(), self.workspace.numel(),
+                self.status.data_ptr(),
             ),
             "cb_derotate_keys",
         )
@@ -357,7 +357,8 @@ class HandoffCall:
         nat.check(
             nat.load().cb_map_install_packed(
                 self.mapper._handle, self._stream(), ctypes.byref(self.src_c), ctypes.byref(self.dst_c), self.n,
-                self.workspace.data_ptr(), self.workspace.numel(), self.status.data_ptr(),
+                self.position_start, ctypes.byref(self.dst_rope), self.workspace.data_ptr(),
+                self.workspace.numel(), self.status.data_ptr(),
             ),
             "cb_map_install_packed",
         )

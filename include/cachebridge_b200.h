@@ -178,19 +178,18 @@ CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
  *  cb_derotate_keys: gather the source key rows of every used source layer
  *    through src->slots, remove the source RoPE in FP32 (rope.py:82-89,
  *    mapper.py:143-144) and store BF16 content-space keys in `workspace`
- *    ([used_layers][n_tokens][heads][128]); also store the target RoPE
- *    coefficients of the call's positions in the workspace tail.
+ *    ([used_layers][n_tokens][heads][128]).
  *  cb_map_install_packed: map keys from `workspace` and values from the
- *    source rows, apply bias and target RoPE, and install into dst rows.
+ *    source rows, add the bias, apply the target RoPE and install into dst rows.
  * cb_map_install(...) == cb_derotate_keys(...) then cb_map_install_packed(...)
- * on the same stream, with the same workspace.
+ * on the same stream, with the same workspace and position_start.
  */
 CB_API int cb_derotate_keys(cb_mapper* mapper, void* stream, const cb_rows* src,
                      int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
-                     const cb_rope* dst_rope, void* workspace, size_t workspace_bytes,
-                     int32_t* dev_status);
+                     void* workspace, size_t workspace_bytes, int32_t* dev_status);
 CB_API int cb_map_install_packed(cb_mapper* mapper, void* stream, const cb_rows* src,
-                          const cb_rows* dst, int64_t n_tokens, const void* workspace,
+                          const cb_rows* dst, int64_t n_tokens, int64_t position_start,
+                          const cb_rope* dst_rope, const void* workspace,
                           size_t workspace_bytes, int32_t* dev_status);
 
 /*
