@@ -30,6 +30,7 @@ CB_INDEX_I32 = 32
 CB_INDEX_I64 = 64
 
 CB_MAX_LAYERS = 128
+CB_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 # Every entry point declared in include/cachebridge_b200.h (checked by tests).
 EXPORTED_SYMBOLS = (
@@ -42,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "cb_mapper_workspace_bytes",
     "cb_rope_table",
     "cb_map_install",
+    "cb_map_install_noalloc",
     "cb_derotate_keys",
     "cb_map_install_packed",
     "cb_pack_rows",
@@ -121,6 +123,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_map_install.argtypes = [
         c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp, c_size, c_vp
     ]
+    lib.cb_map_install_noalloc.restype = c_int
+    lib.cb_map_install_noalloc.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp]
     lib.cb_derotate_keys.restype = c_int
     lib.cb_derotate_keys.argtypes = [c_vp, c_vp, rows_p, c_i64, c_i64, rope_p, c_vp, c_size, c_vp]
     lib.cb_map_install_packed.restype = c_int

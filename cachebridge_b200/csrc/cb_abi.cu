@@ -716,3 +716,75 @@ int cb_enable_peer_access(int device, int peer) {
 }
 
 }  // extern "C"
+
+// ------------------------- no-allocation map + install -------------------------
+// cb_map_install_noalloc: cb_map_install with its key workspace taken from a
+// fixed device array that belongs to this library instead of from the caller.
+// It serves callers that cannot allocate device memory at handoff time: a
+// serving engine that sized its KV pool to fill the GPU at start-up and so has
+// no headroom left for per-handoff scratch, and hosts that bind the C ABI
+// without any device allocator of their own (an FFI caller holding only raw
+// pointers), where a cudaMalloc/cudaFree pair per call would also stall the
+// device. The array is CB_NOALLOC_SCRATCH_BYTES (64 MiB) per device; it holds
+// the BF16 content-space keys [used_layers][n_tokens][heads][128], so one call
+// maps at most 64 MiB / (used_layers * heads * 256 B) tokens. Every call on a
+// device shares it, so calls whose GPU work overlaps (unordered streams,
+// concurrent host threads) race on it. No part of it must start at zero: the
+// key phase writes every element that the map phase reads.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device`, which the caller has made
+// current. Looked up once per device, on that device's first call.
+int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(CB_ERR_UNSUPPORTED, "cb_map_install_noalloc: device index beyond the 64 this build tracks");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_ptr[device] = ptr;
+  }
+  *out = g_noalloc_ptr[device];
+  return CB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cb_map_install_noalloc(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
+                           int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
+                           const cb_rope* dst_rope, int dtype, int32_t* dev_status) {
+  if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
+  if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
+  const size_t need = cb_mapper_workspace_bytes(m, dtype, n_tokens);
+  if (need > static_cast<size_t>(CB_NOALLOC_SCRATCH_BYTES)) {
+    const size_t per_token = cb_mapper_workspace_bytes(m, dtype, 1);
+    char msg[320];
+    std::snprintf(msg, sizeof msg,
+                  "cb_map_install_noalloc: %lld tokens need %zu bytes of key scratch, above its fixed %d bytes "
+                  "(at most %zu tokens per call for this mapper); split the tokens over several calls or use "
+                  "cb_map_install with a caller workspace",
+                  static_cast<long long>(n_tokens), need, CB_NOALLOC_SCRATCH_BYTES,
+                  per_token ? static_cast<size_t>(CB_NOALLOC_SCRATCH_BYTES) / per_token : size_t(0));
+    return fail(CB_ERR_UNSUPPORTED, msg);
+  }
+  void* scratch = nullptr;
+  {
+    DeviceGuard guard(m->device);
+    if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+    const int rc = noalloc_scratch(m->device, &scratch);
+    if (rc != CB_OK) return rc;
+  }
+  return cb_map_install(m, stream, src, dst, n_tokens, position_start, src_rope, dst_rope, dtype, scratch,
+                        static_cast<size_t>(CB_NOALLOC_SCRATCH_BYTES), dev_status);
+}
+
+}  // extern "C"

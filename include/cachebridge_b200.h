@@ -172,6 +172,31 @@ CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
                    size_t workspace_bytes, int32_t* dev_status);
 
 /*
+ * cb_map_install without a caller workspace; no counterpart in the reference.
+ * For callers that cannot allocate device memory when a handoff runs: a
+ * serving engine whose KV pool was sized at start-up to fill the GPU, or an
+ * FFI host that holds raw device pointers but no device allocator. The key
+ * workspace is instead a fixed array of CB_NOALLOC_SCRATCH_BYTES (64 MiB) per
+ * device inside this library, so one call maps at most
+ * CB_NOALLOC_SCRATCH_BYTES / cb_mapper_workspace_bytes(mapper, dtype, 1)
+ * tokens; a larger n_tokens is rejected with CB_ERR_UNSUPPORTED before any
+ * work is queued. The call itself allocates nothing (no cudaMalloc, cudaFree
+ * or allocating library routine). Its first call on a device performs a
+ * one-time set-up (cudaGetSymbolAddress of the array, which can make CUDA
+ * load this library's device code on that device); make that first call
+ * before any stream capture. Every call on a device shares the one array:
+ * calls whose GPU work can overlap (streams not ordered with one another,
+ * concurrent host threads) race on it and must be serialised by the caller.
+ * Nothing in the array needs to start at zero. Arguments and results are
+ * those of cb_map_install.
+ */
+#define CB_NOALLOC_SCRATCH_BYTES (64 << 20)
+CB_API int cb_map_install_noalloc(cb_mapper* mapper, void* stream, const cb_rows* src,
+                           const cb_rows* dst, int64_t n_tokens, int64_t position_start,
+                           const cb_rope* src_rope, const cb_rope* dst_rope, int dtype,
+                           int32_t* dev_status);
+
+/*
  * The two phases of cb_map_install's tensor-core path as separate calls
  * (head_dim 128, BF16 storage only), mirroring the reference's pack -> map
  * split (online/blocks.py:47-82 then mapper.py:116-239):
