@@ -360,9 +360,12 @@ def run_single(args):
     cpu_value, cores = cpu_reference_tokens_per_s(layers, n_sample=args.cpu_tokens, reps=2)
 
     hbm_peak, tc_peak, peak_kind = measured_peaks()
-    tc_avg_s = statistics.mean(tc_ms) / 1e3
-    achieved = bytes_alg / tc_avg_s / 1e9
-    traffic = profiled_traffic("map_install_tc_cfg2_traffic")
+    # The handoff's algorithmic bytes are moved by its two launches together
+    # (key gather/derotation, then the fused map/install), so the roofline is
+    # taken over one handoff: both launches' device time.
+    step_avg_s = statistics.mean(step_ms) / 1e3
+    achieved = bytes_alg / step_avg_s / 1e9
+    traffic = profiled_traffic("handoff_cfg2_traffic")
     line = dict(
         metric=METRIC, value=value, unit=UNIT, n_gpus=1, steps=args.steps, warmup=args.warmup,
         ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
@@ -373,9 +376,11 @@ def run_single(args):
                     parallelism="single GPU (source and target pools on one device)"),
         latency_p50_ms=statistics.median(step_ms),
         roofline=dict(bound="hbm", achieved=achieved, peak=hbm_peak, unit="GB/s", frac=achieved / hbm_peak,
-                      traffic=None if traffic is None else traffic.get("dram_bytes_per_launch"),
-                      kernel="map_install_tc_kernel", algorithmic_bytes=bytes_alg, peak_source=peak_kind,
-                      tensor_tflops=flops / tc_avg_s / 1e12, tensor_frac=flops / tc_avg_s / 1e12 / tc_peak),
+                      traffic=None if traffic is None else traffic.get("dram_bytes_per_step"),
+                      kernel="derotate_pack_kernel + map_install_tc_kernel (one handoff)",
+                      algorithmic_bytes=bytes_alg, peak_source=peak_kind,
+                      tensor_tflops=flops / step_avg_s / 1e12, tensor_frac=flops / step_avg_s / 1e12 / tc_peak,
+                      roofline_ms=1e3 * max(bytes_alg / (hbm_peak * 1e9), flops / (tc_peak * 1e12))),
         kernels_ms=dict(map_install_tc=statistics.mean(tc_ms), derotate_pack=statistics.mean(pre_ms)),
         cpu_baseline=dict(value=cpu_value, unit=UNIT, cores=cores, kind="port",
                           sample=f"{args.cpu_tokens}-token block of the same workload (40->64 layers, 8 heads), "
@@ -390,6 +395,172 @@ def run_single(args):
     return 0
 
 
+# ----------------------------------------------------------------------------
+# N > 1: BASELINE config 3 (source TP N/2 + target TP N/2, peer stores)
+# ----------------------------------------------------------------------------
+def run_sharded(args):
+    import datetime
+
+    import torch.distributed as dist
+
+    import cachebridge_b200 as cb
+    from cachebridge_b200.online import tp
+    from cachebridge_b200.online.blocks import map_install_block
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch one rank per GPU with torchrun")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    host_group = dist.new_group(backend="gloo")
+    L_s, L_t, H, D, S, theta = (QWEN[k] for k in ("L_s", "L_t", "H", "D", "S", "theta"))
+    plan = tp.pair_plan(world, rank, H)
+    Hr = plan.heads_per_rank
+    n_req, n_tok, chunk = args.requests, args.request_tokens, args.chunk
+    total = n_req * n_tok
+    rows = total + args.pool_slack
+    # Both ranks of a pair draw the same slot lists.
+    g = torch.Generator().manual_seed(1000 + plan.tp_rank)
+    src_perm = torch.randperm(rows, generator=g)[:total]
+    dst_perm = torch.randperm(rows, generator=g)[:total]
+    mapper = src_pool = dst_pool = handoff = None
+    if plan.role == "source":
+        layers = random_layers(L_s=L_s, L_t=L_t, H=H, D=D, S=S, seed=11)
+        mapper = cb.PageMapper.from_tensors(layers, method="cachebridge", source_rope_theta=theta,
+                                            target_rope_theta=theta, device=dev, target_tp_rank=plan.tp_rank,
+                                            target_tp_size=plan.tp)
+        log(f"rank {rank}: source pool {L_s} layers x {rows} rows x {Hr} heads")
+        src_pool = cb.TokenKVPool(layers=L_s, rows=rows, heads=Hr, head_dim=D, device=dev)
+        gd = torch.Generator(device=dev).manual_seed(17 + plan.tp_rank)
+        for buf in (src_pool.k_buffer, src_pool.v_buffer):
+            buf.normal_(generator=gd)
+            buf.mul_(torch.exp(0.5 * torch.randn(L_s, 1, Hr, D, generator=gd, device=dev)).to(buf.dtype))
+    else:
+        log(f"rank {rank}: target pool {L_t} layers x {rows} rows x {Hr} heads")
+        dst_pool = cb.TokenKVPool(layers=L_t, rows=rows, heads=Hr, head_dim=D, device=dev)
+    torch.cuda.synchronize()
+    peer_pool = tp.exchange_target_pools(plan, dst_pool, group=host_group, device=dev)
+    requests = [(src_perm[q * n_tok:(q + 1) * n_tok].to(dev), dst_perm[q * n_tok:(q + 1) * n_tok].to(dev))
+                for q in range(n_req)]
+    if plan.role == "source":
+        handoff = tp.ShardedHandoff(mapper, src_pool, peer_pool, requests, chunk=chunk,
+                                    source_head_offset=plan.head_start)
+    ones = torch.ones(1, dtype=torch.int32, device=dev)
+
+    def step():
+        if handoff is not None:
+            handoff.run()
+            ready = tp.device_ready(dev)
+        else:
+            ready = ones.clone()
+        return tp.publication_vote(ready, device=dev)
+
+    for _ in range(args.warmup):
+        vote = step()
+    torch.cuda.synchronize()
+    if int(vote.item()) != 1:
+        raise RuntimeError("warm-up handoff was not published (a rank reported a device error)")
+
+    # ---- device-resident timing ------------------------------------------------
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clocks:
+        ev[0].record()
+        for k in range(args.steps):
+            vote = step()
+            ev[k + 1].record()
+        ev[-1].synchronize()
+    published = int(vote.item())
+    per_step = torch.tensor([ev[k].elapsed_time(ev[k + 1]) for k in range(args.steps)] +
+                            [ev[0].elapsed_time(ev[-1]), float(published == 1)], device=dev)
+    dist.all_reduce(per_step[:-1], op=dist.ReduceOp.MAX)
+    dist.all_reduce(per_step[-1:], op=dist.ReduceOp.MIN)
+    step_ms, total_ms, all_published = per_step[:-2].tolist(), float(per_step[-2]), float(per_step[-1])
+    if all_published != 1.0:
+        raise RuntimeError("sharded handoff was not published on every rank")
+
+    # ---- end to end through the public API --------------------------------------
+    # Per step: the requests' slot tables come from pinned host memory, every
+    # chunk goes through map_install_block (RowSet marshalling, validation and
+    # launches), and the published vote is read back to the host.
+    host_idx = [(s.cpu().pin_memory(), t.cpu().pin_memory()) for s, t in requests]
+    dev_idx = [(torch.empty_like(s, device=dev), torch.empty_like(t, device=dev)) for s, t in host_idx]
+    vote_host = torch.empty(1, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        for (hs, ht), (ds, dt) in zip(host_idx, dev_idx):
+            ds.copy_(hs, non_blocking=True)
+            dt.copy_(ht, non_blocking=True)
+        if plan.role == "source":
+            for ds, dt in dev_idx:
+                for a, b in tp.chunk_spans(n_tok, chunk):
+                    map_install_block(mapper, src_pool, ds, peer_pool, dt, start=a, stop=b,
+                                      source_head_offset=plan.head_start, target_head_offset=0)
+            ready = tp.device_ready(dev)
+        else:
+            ready = ones.clone()
+        vote_host.copy_(tp.publication_vote(ready, device=dev), non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    e_ev[0].record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e_ev[1].record()
+    e_ev[1].synchronize()
+    e2e_ms = torch.tensor([e_ev[0].elapsed_time(e_ev[1]) / args.e2e_steps], device=dev)
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    if int(vote_host.item()) != 1:
+        raise RuntimeError("end-to-end handoff was not published")
+
+    launches = torch.tensor([handoff.launches * args.steps if handoff else 0], device=dev)
+    dist.all_reduce(launches)
+    clk = clocks.summary()
+    value = total * args.steps / (total_ms / 1e3)
+    shard_bytes = total * 2 * L_t * Hr * D * 2  # mapped rows crossing NVLink per pair per step
+    nvlink_peak = 770.0  # measured peer copy per direction on this pool's B200s (GB/s)
+    achieved = shard_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
+    if rank == 0:
+        h2d = sum(s.numel() * s.element_size() + t.numel() * t.element_size() for s, t in host_idx)
+        line = dict(
+            metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="strong", vs_baseline=None,
+            dtype="bf16", data="synthetic",
+            config=dict(workload=f"qwen3-14b->32b sharded handoff (BASELINE config 3), TP{plan.tp}+TP{plan.tp}",
+                        requests=n_req, request_tokens=n_tok, chunk_tokens=chunk, source_layers=L_s,
+                        target_layers=L_t, kv_heads=H, heads_per_rank=Hr, head_dim=D, selected=S,
+                        pool_slots=rows, page_size=1, slot_lists="seeded random",
+                        transport="map kernel stores into the peer pool (CUDA IPC, NVLink)",
+                        l2="inputs larger than L2", parallelism=f"src tp{plan.tp} -> dst tp{plan.tp}"),
+            latency_p50_ms=statistics.median(step_ms),
+            roofline=dict(bound="nvlink", achieved=achieved, peak=nvlink_peak, unit="GB/s",
+                          frac=achieved / nvlink_peak, traffic=None,
+                          kernel="map_install_tc_kernel peer stores (one pair, per direction)",
+                          shard_bytes_per_pair=shard_bytes, peak_source="recipe-measured peer copy"),
+            cpu_baseline=None,
+            e2e=dict(value=total / (float(e2e_ms) / 1e3), unit=UNIT, h2d_bytes_per_step=h2d,
+                     d2h_bytes_per_step=4,
+                     path="slot tables H2D + map_install_block per chunk into the peer pool + vote D2H",
+                     ms_per_step=float(e2e_ms)),
+            gpu_launches=int(launches.item()),
+            clocks=clk,
+        )
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if peer_pool is not None:
+        peer_pool.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -401,6 +572,10 @@ def main(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-tokens", type=int, default=2048)
     ap.add_argument("--ref-tokens", type=int, default=2048)
+    ap.add_argument("--requests", type=int, default=16, help="requests per step (N>1)")
+    ap.add_argument("--request-tokens", type=int, default=32768, help="history tokens per request (N>1)")
+    ap.add_argument("--chunk", type=int, default=2048, help="tokens per map+install call (N>1)")
+    ap.add_argument("--pool-slack", type=int, default=4096, help="free pool rows beyond the requests (N>1)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         log("warm-up raised to 3 steps (timing rule)")
@@ -409,9 +584,7 @@ def main(argv=None):
         return run_reference(args)
     if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         return run_single(args)
-    from cachebridge_b200.tp_bench import run_sharded
-
-    return run_sharded(args, METRIC, UNIT, QWEN)
+    return run_sharded(args)
 
 
 if __name__ == "__main__":

@@ -134,7 +134,7 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_install_rows.restype = c_int
     lib.cb_install_rows.argtypes = [c_vp, c_vp, rows_p, c_int, c_int, c_i64, c_vp]
     lib.cb_ipc_export.restype = c_int
-    lib.cb_ipc_export.argtypes = [c_vp, c_vp]
+    lib.cb_ipc_export.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]
     lib.cb_ipc_open.restype = c_int
     lib.cb_ipc_open.argtypes = [c_vp, c_int, ctypes.POINTER(c_vp)]
     lib.cb_ipc_close.restype = c_int

@@ -55,6 +55,54 @@ uint16_t f32_to_bf16_rne(float f) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Rows or blocks may live on another GPU (a target pool opened through CUDA
+// IPC, a peer staging block). Kernels on `device` can only touch them once
+// peer access device -> owner is enabled, so every launch that takes such a
+// pointer enables it first (once per device pair) or refuses the call.
+constexpr int kMaxPeerDevices = 64;
+std::mutex g_peer_mu;
+bool g_peer_on[kMaxPeerDevices][kMaxPeerDevices] = {};
+
+int ensure_access(int device, const void* ptr, const char* what) {
+  cudaPointerAttributes a{};
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(CB_ERR_INVALID, std::string(what) + ": not a CUDA pointer");
+  }
+  if (a.type == cudaMemoryTypeManaged) return CB_OK;
+  if (a.type != cudaMemoryTypeDevice) return fail(CB_ERR_INVALID, std::string(what) + ": must be device memory");
+  if (a.device == device) return CB_OK;
+  if (device < 0 || device >= kMaxPeerDevices || a.device < 0 || a.device >= kMaxPeerDevices)
+    return fail(CB_ERR_UNSUPPORTED, std::string(what) + ": device index beyond the 64 this build tracks");
+  std::lock_guard<std::mutex> lock(g_peer_mu);
+  if (g_peer_on[device][a.device]) return CB_OK;
+  int can = 0;
+  e = cudaDeviceCanAccessPeer(&can, device, a.device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+  if (!can)
+    return fail(CB_ERR_UNSUPPORTED, std::string(what) + ": lives on device " + std::to_string(a.device) +
+                                        ", which device " + std::to_string(device) + " cannot access");
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  e = cudaDeviceEnablePeerAccess(a.device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+  } else if (e != cudaSuccess) {
+    return cuda_fail(e, "cudaDeviceEnablePeerAccess");
+  }
+  g_peer_on[device][a.device] = true;
+  return CB_OK;
+}
+
+// Peer access for the first K and V buffers of a row set (the layers of one
+// row set share a device).
+int ensure_rows_access(int device, const cb_rows* r, const char* what) {
+  int rc = ensure_access(device, r->k[0], what);
+  if (rc != CB_OK) return rc;
+  return ensure_access(device, r->v[0], what);
+}
+
 int elem_size(int dtype) { return dtype == CB_DTYPE_F32 ? 4 : 2; }
 
 int check_rows(const cb_rows* r, const char* name, int head_dim, int heads_used, int dtype,
@@ -502,6 +550,8 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
+  if ((rc = ensure_rows_access(m->device, dst, "dst rows")) != CB_OK) return rc;
 
   if (tc) {
     if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
@@ -561,6 +611,7 @@ int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_t
   if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
   return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, position_start, src_rope, workspace,
                          dev_status);
 }
@@ -576,6 +627,8 @@ int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const 
   if ((rc = check_tc_extras(m, CB_DTYPE_BF16, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
   DeviceGuard guard(m->device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
+  if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
+  if ((rc = ensure_rows_access(m->device, dst, "dst rows")) != CB_OK) return rc;
   return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, position_start, dst_rope, workspace,
                    dev_status);
 }
@@ -611,6 +664,12 @@ int cb_pack_rows(void* stream, const cb_rows* src, int head_dim, int dtype, int6
   if (rc != CB_OK) return rc;
   if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
   if (n_tokens > 0 && out == nullptr) return fail(CB_ERR_INVALID, "null output block");
+  if (n_tokens > 0) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(CB_ERR_CUDA, "cudaGetDevice failed");
+    if ((rc = ensure_rows_access(device, src, "src rows")) != CB_OK) return rc;
+    if ((rc = ensure_access(device, out, "output block")) != CB_OK) return rc;
+  }
   const int es = elem_size(dtype);
   cbk::CopyRowsParams p{};
   p.layers = src->layers;
@@ -646,6 +705,12 @@ int cb_install_rows(void* stream, const void* block, const cb_rows* dst, int hea
   if (rc != CB_OK) return rc;
   if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
   if (n_tokens > 0 && block == nullptr) return fail(CB_ERR_INVALID, "null source block");
+  if (n_tokens > 0) {
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail(CB_ERR_CUDA, "cudaGetDevice failed");
+    if ((rc = ensure_access(device, block, "source block")) != CB_OK) return rc;
+    if ((rc = ensure_rows_access(device, dst, "dst rows")) != CB_OK) return rc;
+  }
   const int es = elem_size(dtype);
   cbk::CopyRowsParams p{};
   p.layers = dst->layers;
@@ -671,13 +736,31 @@ int cb_install_rows(void* stream, const void* block, const cb_rows* dst, int hea
   return launch_copy_rows(static_cast<cudaStream_t>(stream), p, n_tokens);
 }
 
-int cb_ipc_export(const void* device_ptr, void* handle_out) {
-  if (device_ptr == nullptr || handle_out == nullptr) return fail(CB_ERR_INVALID, "null pointer");
+int cb_ipc_export(const void* device_ptr, void* handle_out, uint64_t* offset_out) {
+  if (device_ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(CB_ERR_INVALID, "null pointer");
+  // The handle names the whole allocation that holds device_ptr (a caching
+  // allocator hands out pieces of larger ones): report where inside it the
+  // pointer sits.
+  static PFN_cuMemGetAddressRange_v3020 range = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(ptr);
+  }();
+  if (range == nullptr) return fail(CB_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(device_ptr)) != CUDA_SUCCESS)
+    return fail(CB_ERR_INVALID, "cb_ipc_export: pointer is not inside a device allocation");
   cudaIpcMemHandle_t h;
-  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr));
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
   if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
   static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
   std::memcpy(handle_out, &h, 64);
+  *offset_out = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(device_ptr) - base);
   return CB_OK;
 }
 

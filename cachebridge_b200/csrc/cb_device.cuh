@@ -186,7 +186,7 @@ __device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uin
       : "memory");
 }
 
-// TMA tiled load of a 4-D box into this CTA's shared memory (no multicast).
+// TMA tiled load of a 4-D box into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
   asm volatile(
@@ -196,31 +196,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// TMA gather of 4 rows (y0..y3, one-row box starting at column x) of a 2-D
-// tensor into 4 consecutive box rows of this CTA's shared memory (no multicast).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, int y0, int y1, int y2,
-                                            int y3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar)
-      : "memory");
-}
-
-// L2 prefetches of the same boxes (no shared memory, no completion tracking).
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_gather4(const CUtensorMap* map, int x, int y0, int y1, int y2, int y3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-               : "memory");
-}
 
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;

@@ -113,8 +113,6 @@ class RowSet:
             require_cuda(self.slots, "slot indices")
             if self.slots.ndim != 1:
                 raise ValueError("one-dimensional integer pool indices required")
-            if self.slots.device != self.device:
-                raise ValueError("pool, indices and workspace must share device and dtype as applicable")
             if not self.slots.is_contiguous():
                 self.slots = self.slots.contiguous()
         return int(stride)
@@ -130,6 +128,55 @@ class RowSet:
             k=ctypes.cast(karr, ctypes.POINTER(ctypes.c_void_p)),
             v=ctypes.cast(varr, ctypes.POINTER(ctypes.c_void_p)),
             row_stride=stride,
+            rows=self.rows,
+            head_offset=self.head_offset,
+            slot_dtype=slot_code(self.slots),
+            slots=None if self.slots is None else self.slots.data_ptr(),
+        )
+
+
+@dataclass
+class RawRows:
+    """Per-layer row buffers given by raw device addresses (no torch tensors).
+
+    For rows this process did not allocate, such as a peer GPU's target pool
+    mapped through CUDA IPC (``cb_ipc_open``); ``device`` is the GPU whose
+    kernels address them, ``slots`` live on that device. Same interface as
+    ``RowSet`` towards the mapper and the C ABI.
+    """
+
+    k_ptrs: list
+    v_ptrs: list
+    heads: int
+    head_dim: int
+    rows: int
+    row_stride: int
+    dtype: torch.dtype
+    device: torch.device
+    head_offset: int = 0
+    slots: torch.Tensor | None = None
+    _keep: list = field(default_factory=list, repr=False)
+
+    @property
+    def layers(self) -> int:
+        return len(self.k_ptrs)
+
+    def to_c(self) -> nat.CbRows:
+        if self.slots is not None:
+            require_cuda(self.slots, "slot indices")
+            if self.slots.ndim != 1:
+                raise ValueError("one-dimensional integer pool indices required")
+            if not self.slots.is_contiguous():
+                self.slots = self.slots.contiguous()
+        karr = nat.pointer_array(self.k_ptrs)
+        varr = nat.pointer_array(self.v_ptrs)
+        self._keep.extend([karr, varr])
+        return nat.CbRows(
+            layers=self.layers,
+            heads=self.heads,
+            k=ctypes.cast(karr, ctypes.POINTER(ctypes.c_void_p)),
+            v=ctypes.cast(varr, ctypes.POINTER(ctypes.c_void_p)),
+            row_stride=self.row_stride,
             rows=self.rows,
             head_offset=self.head_offset,
             slot_dtype=slot_code(self.slots),

@@ -234,6 +234,9 @@ class PageMapper:
             raise ValueError("mapper selected layer exceeds source page depth")
         if dst.layers != self.target_layers or src.dtype != dst.dtype:
             raise ValueError("mapper output geometry/dtype mismatch")
+        for rs in (src, dst):
+            if rs.slots is not None and rs.slots.device != self.device:
+                raise ValueError("pool, indices and workspace must share device and dtype as applicable")
         n = int(n_tokens)
         if (src.slots is not None and src.slots.numel() < n) or (dst.slots is not None and dst.slots.numel() < n):
             raise ValueError("invalid target range or non-CacheBridge method")

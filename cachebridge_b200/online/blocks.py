@@ -138,7 +138,10 @@ def map_install_block(
     src = RowSet.from_pool(source_pool, source_indices[start:stop], head_offset=head_start)
     if not 0 <= head_start < head_start + mapper.heads <= src.heads:
         raise ValueError("Received source shard does not contain required heads")
-    dst = RowSet.from_pool(target_pool, target_indices[start:stop], head_offset=target_head_offset)
+    if hasattr(target_pool, "rows"):  # TokenKVPool, or a peer pool mapped through CUDA IPC
+        dst = target_pool.rows(target_indices[start:stop], target_head_offset)
+    else:
+        dst = RowSet.from_pool(target_pool, target_indices[start:stop], head_offset=target_head_offset)
     if target_head_offset < 0 or target_head_offset + mapper.heads > dst.heads:
         raise ValueError("mapper output geometry/dtype mismatch")
     mapper.map_install(src, dst, n, position_start=start)

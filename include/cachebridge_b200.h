@@ -18,6 +18,11 @@
  *    cb_pack_rows, cb_install_rows, cb_rope_table) never allocate device or
  *    host memory. cb_mapper_create is
  *    the only allocating call besides the IPC helpers.
+ *  - Rows and blocks may live on another GPU of the process (for example a
+ *    target pool opened through CUDA IPC). The first call that meets such a
+ *    pointer enables peer access from the launching device to its owner, or
+ *    fails with CB_ERR_UNSUPPORTED when the two devices cannot reach each
+ *    other; kernels then load and store peer memory directly over NVLink.
  *  - Row indices (slots) are validated on the device: an index outside
  *    [0, rows) is skipped and CB_DEV_ERR_SLOT_RANGE is OR-ed into the caller's
  *    device status word, which the caller reads after the stream completes.
@@ -240,12 +245,19 @@ CB_API int cb_install_rows(void* stream, const void* block, const cb_rows* dst,
                     int32_t* dev_status);
 
 /*
- * CUDA IPC helpers for the tensor-parallel transfer: export a device
- * allocation (64-byte handle) and map a peer's allocation into this process.
- * They stand in for torch's reduce_tensor / rebuild_cuda_tensor used by
- * backends/sglang/runtime/bounded_handoff_channel.py:83-123.
+ * CUDA IPC helpers for the tensor-parallel transfer. They stand in for torch's
+ * reduce_tensor / rebuild_cuda_tensor used by
+ * backends/sglang/runtime/bounded_handoff_channel.py:83-123, with one
+ * difference that matters for kernels: the importer maps the allocation into
+ * the context of the device that will access it (`device`), with lazy peer
+ * access, so a kernel on that device can store into it directly.
+ *  cb_ipc_export: 64-byte handle of the allocation holding device_ptr, and
+ *    the byte offset of device_ptr inside it.
+ *  cb_ipc_open: map a peer allocation on `device`; *ptr_out is its base (add
+ *    the exporter's offset).
+ *  cb_ipc_close: unmap a base returned by cb_ipc_open.
  */
-CB_API int cb_ipc_export(const void* device_ptr, void* handle_out /* 64 bytes */);
+CB_API int cb_ipc_export(const void* device_ptr, void* handle_out /* 64 bytes */, uint64_t* offset_out);
 CB_API int cb_ipc_open(const void* handle /* 64 bytes */, int device, void** ptr_out);
 CB_API int cb_ipc_close(void* ptr);
 /* Enable direct peer access from `device` to `peer` (idempotent). */

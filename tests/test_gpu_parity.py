@@ -321,3 +321,37 @@ def test_rope_table_matches_qwen_rope(cuda_device, theta, scaling, start):
     # frequency-major [D/2, n] against the reference's [n, D] (first half)
     torch.testing.assert_close(cos.cpu().T, ref_cos[:, : D // 2], atol=2e-6, rtol=0)
     torch.testing.assert_close(sin.cpu().T, ref_sin[:, : D // 2], atol=2e-6, rtol=0)
+
+
+def test_padded_destination_rows(tmp_path, cuda_device):
+    """Destination rows padded by 16 bytes (not 32-byte aligned) get the same
+    bytes as an aligned pool, and the padding keeps its canary."""
+    from cachebridge_b200.device import RowSet
+
+    g = torch.Generator().manual_seed(41)
+    L_s, L_t, H, D, n, rows = 6, 4, 2, 128, 300, 700
+    mapper_dir = _random_mapper(tmp_path, seed=12, L_s=L_s, L_t=L_t, H=H, D=D, S=2)
+    src_slots = torch.randperm(rows, generator=g)[:n]
+    dst_slots = torch.randperm(rows, generator=g)[:n]
+    src_pool, _ = _content_pool(g, layers=L_s, rows=rows, heads=H, D=D, dtype=torch.bfloat16, theta=1e6,
+                                positions=torch.arange(n), slots=src_slots, device=cuda_device)
+    mapper = PageMapper(mapper_dir, method="cachebridge", source_rope_theta=1e6, target_rope_theta=1e6,
+                        device=cuda_device)
+    aligned = TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=cuda_device, fill=CANARY)
+    stride = H * D + 8  # 16 bytes of padding per row
+    flat = torch.full((2, L_t, 8 + rows * stride), CANARY, dtype=torch.bfloat16, device=cuda_device)
+    views = [[flat[kind, l, 8:].as_strided((rows, H, D), (stride, D, 1)) for l in range(L_t)] for kind in range(2)]
+    padded = RowSet(views[0], views[1], H, D, 0, dst_slots.to(cuda_device))
+    src = src_pool.rows(src_slots.to(cuda_device))
+    mapper.map_install(src, aligned.rows(dst_slots.to(cuda_device)), n, 0)
+    mapper.map_install(src, padded, n, 0)
+    torch.cuda.synchronize()
+    raise_for_status(cuda_device)
+    for kind, buf in ((0, aligned.k_buffer), (1, aligned.v_buffer)):
+        got = torch.stack([views[kind][l] for l in range(L_t)])
+        assert torch.equal(got[:, dst_slots.to(cuda_device)], buf[:, dst_slots.to(cuda_device)])
+        mask = torch.ones(rows, dtype=torch.bool, device=cuda_device)
+        mask[dst_slots.to(cuda_device)] = False
+        assert bool((got[:, mask].float() == CANARY).all()), "an untouched row changed"
+        pad = flat[kind, :, 8:].reshape(L_t, rows, stride)[:, :, H * D :]
+        assert bool((pad.float() == CANARY).all()) and bool((flat[kind, :, :8].float() == CANARY).all())
