@@ -422,16 +422,21 @@ def run_sharded(args):
     n_req, n_tok, chunk = args.requests, args.request_tokens, args.chunk
     total = n_req * n_tok
     rows = total + args.pool_slack
+    target_side = args.placement == "target"
     # Both ranks of a pair draw the same slot lists.
     g = torch.Generator().manual_seed(1000 + plan.tp_rank)
     src_perm = torch.randperm(rows, generator=g)[:total]
     dst_perm = torch.randperm(rows, generator=g)[:total]
-    mapper = src_pool = dst_pool = handoff = None
-    if plan.role == "source":
+    requests = [(src_perm[q * n_tok:(q + 1) * n_tok].to(dev), dst_perm[q * n_tok:(q + 1) * n_tok].to(dev))
+                for q in range(n_req)]
+    mapper = src_pool = dst_pool = None
+    if plan.role == "target" or not target_side:
+        # The rank that maps: the target (target placement) or the source.
         layers = random_layers(L_s=L_s, L_t=L_t, H=H, D=D, S=S, seed=11)
         mapper = cb.PageMapper.from_tensors(layers, method="cachebridge", source_rope_theta=theta,
                                             target_rope_theta=theta, device=dev, target_tp_rank=plan.tp_rank,
                                             target_tp_size=plan.tp)
+    if plan.role == "source":
         log(f"rank {rank}: source pool {L_s} layers x {rows} rows x {Hr} heads")
         src_pool = cb.TokenKVPool(layers=L_s, rows=rows, heads=Hr, head_dim=D, device=dev)
         gd = torch.Generator(device=dev).manual_seed(17 + plan.tp_rank)
@@ -442,17 +447,22 @@ def run_sharded(args):
         log(f"rank {rank}: target pool {L_t} layers x {rows} rows x {Hr} heads")
         dst_pool = cb.TokenKVPool(layers=L_t, rows=rows, heads=Hr, head_dim=D, device=dev)
     torch.cuda.synchronize()
-    peer_pool = tp.exchange_target_pools(plan, dst_pool, group=host_group, device=dev)
-    requests = [(src_perm[q * n_tok:(q + 1) * n_tok].to(dev), dst_perm[q * n_tok:(q + 1) * n_tok].to(dev))
-                for q in range(n_req)]
-    if plan.role == "source":
-        handoff = tp.ShardedHandoff(mapper, src_pool, peer_pool, requests, chunk=chunk,
-                                    source_head_offset=plan.head_start)
+    peer_pool = placement = handoff = None
+    if target_side:
+        placement = tp.TargetPlacement(plan, requests, chunk=chunk, source_layers=L_s, device=dev, group=host_group,
+                                       source_pool=src_pool, mapper=mapper, target_pool=dst_pool)
+        runner = placement
+    else:
+        peer_pool = tp.exchange_target_pools(plan, dst_pool, group=host_group, device=dev)
+        if plan.role == "source":
+            handoff = tp.ShardedHandoff(mapper, src_pool, peer_pool, requests, chunk=chunk,
+                                        source_head_offset=plan.head_start)
+        runner = handoff
     ones = torch.ones(1, dtype=torch.int32, device=dev)
 
     def step():
-        if handoff is not None:
-            handoff.run()
+        if runner is not None:
+            runner.run()
             ready = tp.device_ready(dev)
         else:
             ready = ones.clone()
@@ -484,19 +494,22 @@ def run_sharded(args):
         raise RuntimeError("sharded handoff was not published on every rank")
 
     # ---- end to end through the public API --------------------------------------
-    # Per step: the requests' slot tables come from pinned host memory, every
-    # chunk goes through map_install_block (RowSet marshalling, validation and
-    # launches), and the published vote is read back to the host.
+    # Per step: every request's slot tables come from pinned host memory, the
+    # handoff runs through the public entry points (TargetPlacement.run, or
+    # map_install_block per chunk for source placement), and the publication
+    # vote is read back to the host.
     host_idx = [(s.cpu().pin_memory(), t.cpu().pin_memory()) for s, t in requests]
-    dev_idx = [(torch.empty_like(s, device=dev), torch.empty_like(t, device=dev)) for s, t in host_idx]
     vote_host = torch.empty(1, dtype=torch.int32).pin_memory()
 
     def e2e_step():
-        for (hs, ht), (ds, dt) in zip(host_idx, dev_idx):
+        for (hs, ht), (ds, dt) in zip(host_idx, requests):
             ds.copy_(hs, non_blocking=True)
             dt.copy_(ht, non_blocking=True)
-        if plan.role == "source":
-            for ds, dt in dev_idx:
+        if target_side:
+            placement.run()
+            ready = tp.device_ready(dev)
+        elif plan.role == "source":
+            for ds, dt in requests:
                 for a, b in tp.chunk_spans(n_tok, chunk):
                     map_install_block(mapper, src_pool, ds, peer_pool, dt, start=a, stop=b,
                                       source_head_offset=plan.head_start, target_head_offset=0)
@@ -520,15 +533,20 @@ def run_sharded(args):
     if int(vote_host.item()) != 1:
         raise RuntimeError("end-to-end handoff was not published")
 
-    launches = torch.tensor([handoff.launches * args.steps if handoff else 0], device=dev)
+    launches = torch.tensor([runner.launches * args.steps if runner is not None else 0], device=dev)
     dist.all_reduce(launches)
     clk = clocks.summary()
     value = total * args.steps / (total_ms / 1e3)
-    shard_bytes = total * 2 * L_t * Hr * D * 2  # mapped rows crossing NVLink per pair per step
+    # Bytes that must cross NVLink per pair per step: raw source rows (target
+    # placement) or mapped target rows (source placement).
+    shard_bytes = total * 2 * (L_s if target_side else L_t) * Hr * D * 2
     nvlink_peak = 770.0  # measured peer copy per direction on this pool's B200s (GB/s)
     achieved = shard_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     if rank == 0:
         h2d = sum(s.numel() * s.element_size() + t.numel() * t.element_size() for s, t in host_idx)
+        transport = ("source rows packed into the target GPU's receive slots (peer stores, CUDA IPC), mapped and "
+                     "installed on the target" if target_side else
+                     "map kernel stores into the peer target pool (CUDA IPC, NVLink)")
         line = dict(
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="strong", vs_baseline=None,
@@ -536,18 +554,20 @@ def run_sharded(args):
             config=dict(workload=f"qwen3-14b->32b sharded handoff (BASELINE config 3), TP{plan.tp}+TP{plan.tp}",
                         requests=n_req, request_tokens=n_tok, chunk_tokens=chunk, source_layers=L_s,
                         target_layers=L_t, kv_heads=H, heads_per_rank=Hr, head_dim=D, selected=S,
-                        pool_slots=rows, page_size=1, slot_lists="seeded random",
-                        transport="map kernel stores into the peer pool (CUDA IPC, NVLink)",
-                        l2="inputs larger than L2", parallelism=f"src tp{plan.tp} -> dst tp{plan.tp}"),
+                        pool_slots=rows, page_size=1, slot_lists="seeded random", placement=args.placement,
+                        transport=transport, l2="inputs larger than L2",
+                        parallelism=f"src tp{plan.tp} -> dst tp{plan.tp}"),
             latency_p50_ms=statistics.median(step_ms),
             roofline=dict(bound="nvlink", achieved=achieved, peak=nvlink_peak, unit="GB/s",
                           frac=achieved / nvlink_peak, traffic=None,
-                          kernel="map_install_tc_kernel peer stores (one pair, per direction)",
+                          kernel=("copy_rows_kernel peer stores" if target_side
+                                  else "map_install_tc_kernel peer stores") + " (one pair, per direction)",
                           shard_bytes_per_pair=shard_bytes, peak_source="recipe-measured peer copy"),
             cpu_baseline=None,
             e2e=dict(value=total / (float(e2e_ms) / 1e3), unit=UNIT, h2d_bytes_per_step=h2d,
                      d2h_bytes_per_step=4,
-                     path="slot tables H2D + map_install_block per chunk into the peer pool + vote D2H",
+                     path=("slot tables H2D + TargetPlacement.run + vote D2H" if target_side else
+                           "slot tables H2D + map_install_block per chunk into the peer pool + vote D2H"),
                      ms_per_step=float(e2e_ms)),
             gpu_launches=int(launches.item()),
             clocks=clk,
@@ -556,6 +576,8 @@ def run_sharded(args):
     torch.cuda.synchronize()
     if peer_pool is not None:
         peer_pool.close()
+    if placement is not None:
+        placement.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0
@@ -576,6 +598,8 @@ def main(argv=None):
     ap.add_argument("--request-tokens", type=int, default=32768, help="history tokens per request (N>1)")
     ap.add_argument("--chunk", type=int, default=2048, help="tokens per map+install call (N>1)")
     ap.add_argument("--pool-slack", type=int, default=4096, help="free pool rows beyond the requests (N>1)")
+    ap.add_argument("--placement", choices=["target", "source"], default="target",
+                    help="N>1: map on the target GPU (raw source rows cross NVLink) or on the source GPU")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         log("warm-up raised to 3 steps (timing rule)")

@@ -782,6 +782,33 @@ int cb_ipc_close(void* ptr) {
   return CB_OK;
 }
 
+int cb_chunk_signal(void* stream, int64_t* flag, int64_t value) {
+  if (flag == nullptr) return fail(CB_ERR_INVALID, "null flag");
+  if (reinterpret_cast<uintptr_t>(flag) % 8) return fail(CB_ERR_INVALID, "flag not 8-byte aligned");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(CB_ERR_CUDA, "cudaGetDevice failed");
+  int rc = ensure_access(device, flag, "flag");
+  if (rc != CB_OK) return rc;
+  cudaError_t e = cbk::launch_signal(reinterpret_cast<unsigned long long*>(flag), value,
+                                     static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "signal launch");
+  return CB_OK;
+}
+
+int cb_chunk_wait(void* stream, const int64_t* flag, int64_t value, int64_t timeout_ns, int32_t* dev_status) {
+  if (flag == nullptr || dev_status == nullptr) return fail(CB_ERR_INVALID, "null flag or status");
+  if (reinterpret_cast<uintptr_t>(flag) % 8) return fail(CB_ERR_INVALID, "flag not 8-byte aligned");
+  if (timeout_ns <= 0) return fail(CB_ERR_INVALID, "timeout must be positive");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(CB_ERR_CUDA, "cudaGetDevice failed");
+  int rc = ensure_access(device, flag, "flag");
+  if (rc != CB_OK) return rc;
+  cudaError_t e = cbk::launch_wait(reinterpret_cast<const unsigned long long*>(flag), value, timeout_ns,
+                                   dev_status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "wait launch");
+  return CB_OK;
+}
+
 int cb_enable_peer_access(int device, int peer) {
   DeviceGuard guard(device);
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");

@@ -277,4 +277,49 @@ cudaError_t launch_map_simt(bool fp32_storage, const SimtParams& p, dim3 grid, s
   return cudaGetLastError();
 }
 
+// ------------------------- cross-GPU chunk handshake -------------------------
+// One-thread kernels that order a chunk pipeline between two GPUs through a
+// 64-bit counter in device memory (the counter may be a peer's, mapped
+// through CUDA IPC). They replace the reference's per-block ready / ACK
+// messages over a Unix socket (source_mapper_adapter.py:197-232
+// _DoubleBufferedSender.offer, :282-324 _DoubleBufferedReceiver.next /
+// acknowledge) with device-side signals, so no host round trip sits between
+// chunks.
+
+// Publish `value` after every write of the preceding kernels on this stream:
+// the fence orders them (system scope, peers included) before the store.
+__global__ void signal_kernel(unsigned long long* flag, long long value) {
+  __threadfence_system();
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(flag), "l"(value) : "memory");
+}
+
+// Wait until *flag >= value (acquire, system scope). Bounded: after
+// timeout_ns the kernel records CB_DEV_ERR_TIMEOUT and returns, so a lost peer
+// ends the pipeline with an error instead of a hung stream.
+__global__ void wait_kernel(const unsigned long long* flag, long long value, long long timeout_ns,
+                            int32_t* status) {
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    long long v;
+    asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    if (v >= value) return;
+    if (static_cast<long long>(global_timer_ns() - t0) > timeout_ns) {
+      flag_error(status, CB_DEV_ERR_TIMEOUT);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+cudaError_t launch_signal(unsigned long long* flag, long long value, cudaStream_t st) {
+  signal_kernel<<<1, 1, 0, st>>>(flag, value);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait(const unsigned long long* flag, long long value, long long timeout_ns, int32_t* status,
+                        cudaStream_t st) {
+  wait_kernel<<<1, 1, 0, st>>>(flag, value, timeout_ns, status);
+  return cudaGetLastError();
+}
+
 }  // namespace cbk

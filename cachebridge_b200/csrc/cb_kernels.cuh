@@ -81,6 +81,9 @@ __global__ void derotate_pack_kernel(const __grid_constant__ DerotateParams p);
 // Host launchers for the templated kernels (kept in the defining translation unit).
 // vec_bytes in {16, 8, 4, 2}.
 cudaError_t launch_copy_rows(int vec_bytes, const CopyRowsParams& p, int blocks, cudaStream_t stream);
+cudaError_t launch_signal(unsigned long long* flag, long long value, cudaStream_t stream);
+cudaError_t launch_wait(const unsigned long long* flag, long long value, long long timeout_ns, int32_t* status,
+                        cudaStream_t stream);
 cudaError_t launch_map_simt(bool fp32_storage, const SimtParams& p, dim3 grid, size_t smem_bytes,
                             cudaStream_t stream);
 

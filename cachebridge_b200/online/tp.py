@@ -215,3 +215,175 @@ class ShardedHandoff:
         """Enqueue every chunk on the current stream."""
         for call in self.calls:
             call.run()
+
+
+class _Mapped:
+    """A peer allocation (or part of one) mapped into this process for ``device``."""
+
+    def __init__(self, exported: tuple, device: torch.device):
+        from .. import _native as nat
+
+        handle, offset = exported
+        self._lib = nat.load()
+        self.device = device
+        base = ctypes.c_void_p()
+        nat.check(self._lib.cb_ipc_open(ctypes.create_string_buffer(handle, 64), device.index, ctypes.byref(base)),
+                  "cb_ipc_open")
+        self.base = base.value
+        self.ptr = base.value + offset
+
+    def close(self) -> None:
+        from .. import _native as nat
+
+        if self.base is not None:
+            with torch.cuda.device(self.device):
+                nat.check(self._lib.cb_ipc_close(ctypes.c_void_p(self.base)), "cb_ipc_close")
+            self.base = None
+
+
+def _export(t: torch.Tensor) -> tuple:
+    from .. import _native as nat
+
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_uint64()
+    nat.check(nat.load().cb_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, ctypes.byref(offset)), "cb_ipc_export")
+    return handle.raw, int(offset.value)
+
+
+class TargetPlacement:
+    """Target-side placement for one source/target pair.
+
+    The source rank gathers each chunk's raw source KV rows (its H_r heads of
+    every source layer) and stores them contiguously into one of two receive
+    slots on the target GPU (``cb_pack_rows`` with a peer output: coalesced
+    NVLink stores); the target rank maps the received block into its own pool
+    (``cb_map_install``: derotation, map, target RoPE, install through the
+    slot table). Raw source rows are 2*L_s*H_r*D*2 bytes per token against
+    2*L_t*H_r*D*2 mapped, so fewer bytes cross NVLink than with source-side
+    placement. Slot reuse is ordered on the GPUs by int64 counters
+    (``cb_chunk_signal`` / ``cb_chunk_wait``): the source waits until the
+    target has consumed the chunk that last used a slot, the target waits
+    until the chunk it maps has arrived.
+
+    Reference: target placement of backends/sglang/runtime/receiver_mapping.py:89-242
+    and native_source.py:29-108, with the double-buffered slots of
+    source_mapper_adapter.py:197-232 / 282-324.
+
+    Every rank of the pair builds one with the same ``requests`` (lists of
+    ``(source_slots, target_slots)`` device tensors) and ``chunk``; the source
+    passes ``source_pool``, the target ``mapper`` and ``target_pool``. The
+    constructor is collective over ``group`` (all ranks of the world).
+    """
+
+    SLOTS = 2
+
+    def __init__(self, plan: PairPlan, requests, *, chunk: int, source_layers: int, device: torch.device,
+                 group=None, source_pool=None, mapper=None, target_pool=None, timeout_s: float = 10.0):
+        from .. import _native as nat
+        from ..device import storage_dtype_code
+
+        self.plan = plan
+        self.device = torch.device(device)
+        self.lib = nat.load()
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.chunks = [(q, a, b) for q, (s, _) in enumerate(requests) for a, b in chunk_spans(len(s), chunk)]
+        self.counter = 0  # chunks enqueued so far, over all runs (the signalled values)
+        self.last_use = [-1] * self.SLOTS  # counter of the chunk that last used each slot
+        self.status = status_word(self.device)
+        H, D = plan.heads_per_rank, None
+        if plan.role == "source":
+            D = source_pool.head_dim
+            dtype = source_pool.dtype
+        else:
+            D = target_pool.head_dim
+            dtype = target_pool.dtype
+        self.dtype_code = storage_dtype_code(dtype)
+        self.head_dim = D
+        elem = torch.tensor([], dtype=dtype).element_size()
+        slot_elems = 2 * source_layers * chunk * H * D
+        self.slot_bytes = slot_elems * elem
+        # Counters start at -1: nothing arrived, nothing consumed.
+        flags = torch.full((self.SLOTS,), -1, dtype=torch.int64, device=self.device)
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        if plan.role == "target":
+            self.recv = torch.empty((self.SLOTS, slot_elems), dtype=dtype, device=self.device)
+            payload = dict(recv=_export(self.recv), ready=_export(flags), uuid=uuid)
+        else:
+            payload = dict(consumed=_export(flags), uuid=uuid)
+        self.flags = flags
+        torch.cuda.synchronize(self.device)
+        gathered = [None] * plan.world
+        dist.all_gather_object(gathered, payload, group=group)
+        peer = gathered[plan.peer]
+        if peer["uuid"] == uuid:
+            # The two sides wait on each other's kernels: they must be different GPUs.
+            raise ValueError("source and target ranks of a pair share one GPU; target placement needs two")
+        self._mapped = []
+        if plan.role == "source":
+            recv = _Mapped(peer["recv"], self.device)
+            ready = _Mapped(peer["ready"], self.device)
+            self._mapped = [recv, ready]
+            self.peer_recv = [recv.ptr + s * self.slot_bytes for s in range(self.SLOTS)]
+            self.peer_ready = [ready.ptr + 8 * s for s in range(self.SLOTS)]
+            self.src_rows = []
+            for q, a, b in self.chunks:
+                rs = RowSet.from_pool(source_pool, requests[q][0][a:b])
+                self.src_rows.append((rs, rs.to_c()))
+            self.row_heads = source_pool.heads
+        else:
+            consumed = _Mapped(peer["consumed"], self.device)
+            self._mapped = [consumed]
+            self.peer_consumed = [consumed.ptr + 8 * s for s in range(self.SLOTS)]
+            # One key workspace, sized for the largest chunk, shared in stream order.
+            biggest = max((b - a for _, a, b in self.chunks), default=0)
+            ws = torch.empty(max(mapper.workspace_bytes(dtype, biggest), 16), dtype=torch.uint8, device=self.device)
+            self.calls = []
+            for i, (q, a, b) in enumerate(self.chunks):
+                n = b - a
+                page = self.recv[i % self.SLOTS, : 2 * source_layers * n * H * D].view(2, source_layers, n, H, D)
+                self.calls.append(mapper.prepare(RowSet.from_page(page), target_pool.rows(requests[q][1][a:b]), n, a,
+                                                 workspace=ws))
+
+    @property
+    def launches(self) -> int:
+        """Kernel launches per ``run`` on this rank."""
+        if self.plan.role == "source":
+            return 3 * len(self.chunks)
+        return sum(4 if c.tensor_core else 3 for c in self.calls)
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def run(self) -> None:
+        """Enqueue every chunk of every request on the current stream."""
+        from .. import _native as nat
+
+        st = self._stream()
+        status = self.status.data_ptr()
+        for i in range(len(self.chunks)):
+            c = self.counter
+            slot = i % self.SLOTS  # fixed per chunk: the target's prepared calls read it
+            if self.plan.role == "source":
+                # The chunk that last used this slot must have been consumed.
+                nat.check(self.lib.cb_chunk_wait(st, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot),
+                                                 self.last_use[slot], self.timeout_ns, status), "cb_chunk_wait")
+                rs, crow = self.src_rows[i]
+                nat.check(self.lib.cb_pack_rows(st, ctypes.byref(crow), self.head_dim, self.dtype_code,
+                                                rs.slots.numel(), ctypes.c_void_p(self.peer_recv[slot]), status),
+                          "cb_pack_rows")
+                nat.check(self.lib.cb_chunk_signal(st, ctypes.c_void_p(self.peer_ready[slot]), c),
+                          "cb_chunk_signal")
+            else:
+                nat.check(self.lib.cb_chunk_wait(st, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot), c,
+                                                 self.timeout_ns, status), "cb_chunk_wait")
+                self.calls[i].run()
+                nat.check(self.lib.cb_chunk_signal(st, ctypes.c_void_p(self.peer_consumed[slot]), c),
+                          "cb_chunk_signal")
+            self.last_use[slot] = c
+            self.counter += 1
+
+    def close(self) -> None:
+        """Unmap the peer buffers (after this rank's stream work finished)."""
+        for m in self._mapped:
+            m.close()
+        self._mapped = []

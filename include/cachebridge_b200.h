@@ -260,6 +260,24 @@ CB_API int cb_install_rows(void* stream, const void* block, const cb_rows* dst,
 CB_API int cb_ipc_export(const void* device_ptr, void* handle_out /* 64 bytes */, uint64_t* offset_out);
 CB_API int cb_ipc_open(const void* handle /* 64 bytes */, int device, void** ptr_out);
 CB_API int cb_ipc_close(void* ptr);
+/*
+ * Device-side chunk handshake between two GPUs (the double-buffered
+ * source -> target pipeline). Both launch one thread on the caller's stream
+ * on the current device; `flag` is an 8-byte aligned int64 counter in device
+ * memory, local or a peer's mapped through cb_ipc_open.
+ *  cb_chunk_signal: after all earlier work on `stream`, store `value` into
+ *    *flag with release semantics at system scope.
+ *  cb_chunk_wait: later work on `stream` starts once *flag >= value
+ *    (acquire, system scope). The wait gives up after timeout_ns, ORs
+ *    CB_DEV_ERR_TIMEOUT into *dev_status and lets the stream continue.
+ * They replace the per-block ready / acknowledge messages of
+ * backends/sglang/runtime/source_mapper_adapter.py:197-232 (_DoubleBufferedSender.offer)
+ * and :282-324 (_DoubleBufferedReceiver.next / acknowledge).
+ */
+CB_API int cb_chunk_signal(void* stream, int64_t* flag, int64_t value);
+CB_API int cb_chunk_wait(void* stream, const int64_t* flag, int64_t value, int64_t timeout_ns,
+                         int32_t* dev_status);
+
 /* Enable direct peer access from `device` to `peer` (idempotent). */
 CB_API int cb_enable_peer_access(int device, int peer);
 

@@ -1,6 +1,10 @@
-"""Sharded handoff on two GPUs: source rank 0 maps into target rank 1's pool
-through CUDA IPC peer stores (NVLink); rank 1 maps the same inputs locally and
-the two pools must be bit-identical, untouched rows keeping their canary.
+"""Sharded handoff on two GPUs, both placements:
+  - source placement: rank 0 maps into rank 1's pool through CUDA IPC peer
+    stores (NVLink);
+  - target placement: rank 0 packs raw source rows into rank 1's receive
+    slots, rank 1 maps them into its own pool (device-side chunk handshake).
+Rank 1 then maps the same inputs locally; the two pools must be
+bit-identical, untouched rows keeping their canary.
 
 Needs two visible GPUs; skipped otherwise.
 """
@@ -36,7 +40,7 @@ def _layers(L_s, L_t, H, D, S, seed):
     return out
 
 
-def _worker(rank, port, results):
+def _worker(rank, port, placement, results):
     import datetime
 
     import torch.distributed as dist
@@ -55,7 +59,8 @@ def _worker(rank, port, results):
         g = torch.Generator().manual_seed(3)
         src_perm = torch.randperm(rows, generator=g)[:900]
         dst_perm = torch.randperm(rows, generator=g)[:900]
-        requests = [(src_perm[:700].to(dev), dst_perm[:700].to(dev)), (src_perm[700:].to(dev), dst_perm[700:].to(dev))]
+        # 600 + 300 tokens in 256-token chunks: 5 chunks, an odd count over 2 slots.
+        requests = [(src_perm[:600].to(dev), dst_perm[:600].to(dev)), (src_perm[600:].to(dev), dst_perm[600:].to(dev))]
         layers = _layers(L_s, L_t, H, D, S, seed=5)
         mapper = cb.PageMapper.from_tensors(layers, method="cachebridge", source_rope_theta=1e6,
                                             target_rope_theta=1e6, device=dev)
@@ -65,17 +70,27 @@ def _worker(rank, port, results):
         src_pool.v_buffer.normal_(generator=gd)
         target = cb.TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=dev, fill=CANARY)
         torch.cuda.synchronize()
-        peer = tp.exchange_target_pools(plan, target if plan.role == "target" else None, group=host, device=dev)
+        peer = None
+        if placement == "source":
+            peer = tp.exchange_target_pools(plan, target if plan.role == "target" else None, group=host, device=dev)
+        else:
+            peer = tp.TargetPlacement(plan, requests, chunk=256, source_layers=L_s, device=dev, group=host,
+                                      source_pool=src_pool if plan.role == "source" else None,
+                                      mapper=mapper if plan.role == "target" else None,
+                                      target_pool=target if plan.role == "target" else None, timeout_s=20.0)
         # Every rank reaches the vote, a local failure included (it votes 0).
         error = None
         ready = torch.ones(1, dtype=torch.int32, device=dev)
-        if plan.role == "source":
-            try:
+        try:
+            if placement == "source" and plan.role == "source":
                 tp.ShardedHandoff(mapper, src_pool, peer, requests, chunk=256).run()
-                ready = tp.device_ready(dev)
-            except Exception as exc:  # noqa: BLE001
-                error = repr(exc)
-                ready = torch.zeros(1, dtype=torch.int32, device=dev)
+            elif placement == "target":
+                for _ in range(2):  # two passes: the slot counters carry over
+                    peer.run()
+            ready = tp.device_ready(dev)
+        except Exception as exc:  # noqa: BLE001
+            error = repr(exc)
+            ready = torch.zeros(1, dtype=torch.int32, device=dev)
         vote = int(tp.publication_vote(ready, device=dev).item())
         if vote != 1:  # not published: every rank stops here
             results[rank] = (vote, error)
@@ -102,7 +117,8 @@ def _worker(rank, port, results):
         dist.destroy_process_group()
 
 
-def test_source_rank_installs_into_peer_pool_bit_exactly():
+@pytest.mark.parametrize("placement", ["source", "target"])
+def test_sharded_install_is_bit_exact(placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -111,7 +127,7 @@ def test_source_rank_installs_into_peer_pool_bit_exactly():
     with ctx.Manager() as manager:
         results = manager.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_worker, args=(r, port, results)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, port, placement, results)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
