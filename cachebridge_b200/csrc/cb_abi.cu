@@ -231,6 +231,29 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
   return CB_OK;
 }
 
+// M-tiles per work item of the tensor-core kernel. An item is one (target
+// layer, head, kind) over a run of R m-tiles; its weights and bias are loaded
+// into shared memory once, and the MMA pipeline drains at each item boundary
+// while the next item's weights arrive (about five m-tiles of tensor time).
+// Items are spread round-robin over the persistent CTAs, so the busiest CTA
+// runs ceil(items / grid) of them: pick the R that minimises
+// ceil(items / grid) * (R + 5), i.e. the longest runs that still balance.
+int tc_chunk_mtiles(int64_t n_tokens, int64_t groups, int grid) {
+  const int64_t mt = (n_tokens + cbk::kBM - 1) / cbk::kBM;
+  int best_r = 1;
+  int64_t best_cost = -1;
+  for (int64_t parts = 1; parts <= mt && parts <= 256; ++parts) {
+    const int64_t r = (mt + parts - 1) / parts;
+    const int64_t items = groups * ((mt + r - 1) / r);
+    const int64_t cost = ((items + grid - 1) / grid) * (r + 5);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_r = static_cast<int>(r);
+    }
+  }
+  return best_r;
+}
+
 int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst,
               int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope, const void* workspace,
               int32_t* dev_status) {
@@ -239,7 +262,7 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.L_t = m->L_t;
   p.H = m->H;
   p.S = m->S;
-  p.R = 4;
+  p.R = tc_chunk_mtiles(n_tokens, 2ll * m->H * m->L_t, m->num_sms);
   p.n_chunks = static_cast<int>((n_tokens + p.R * cbk::kBM - 1) / (p.R * cbk::kBM));
   const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
   if (items > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "work too large for one call");
@@ -288,10 +311,6 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
     float max_inv = 0.f;
     for (int i = 0; i < dst_rope->half_dim; ++i) max_inv = std::max(max_inv, std::fabs(dst_rope->inv_freq[i]));
     p.trig_exact = static_cast<double>(position_start + n_tokens) * max_inv > 4.0e5 ? 1 : 0;
-  }
-  for (int k = 0; k < cbk::kTrigEntries; ++k) {
-    const double a = 6.283185307179586476925 * k / cbk::kTrigEntries;
-    p.trig[k] = make_float2(static_cast<float>(std::cos(a)), static_cast<float>(std::sin(a)));
   }
   p.status = dev_status;
   const int smem = cbk::tc_smem_bytes(p.w_slots, p.stages);

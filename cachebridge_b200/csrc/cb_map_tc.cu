@@ -89,7 +89,6 @@ struct Smem {
   uint32_t a;      // A stages
   uint32_t ones;   // constant ones block
   uint8_t* e_gen;  // epilogue staging (generic pointer)
-  const float2* trig;
   uint32_t bars;   // mbarrier array
   uint32_t* tmem_holder;
   volatile int* abort_flag;
@@ -110,25 +109,29 @@ __device__ __forceinline__ uint64_t make_noswizzle_k16_desc(uint32_t smem_addr) 
   return d;  // layout type 0: no swizzle
 }
 
-// Table-driven sin/cos of an FP32 phase (Tang's method): phi = k*(2pi/128) + r
-// by a two-constant Cody-Waite reduction with FMA, |r| <= pi/128 (+ rounding
-// slack), (cos, sin)(2pi k/128) from a 128-entry table, cos(r) and sin(r) from
-// their Taylor series (truncation below 1e-12 for |r| < 0.05). The result is
-// within a few FP32 ulps of cos/sin(phi) for |phi| < 4e5 (k stays an exact
-// FP32 integer); calls with larger phases use sincosf (MapTcParams::trig_exact).
-__device__ __forceinline__ void sincos_tab(float phi, const float2* tab, float& c, float& s) {
-  const float kInvStep = 0x1.45f306p+4f;    // 128 / (2 pi)
-  const float kStepHi = 0x1.921fb6p-5f;     // fl(2 pi / 128)
-  const float kStepLo = -0x1.777a5cp-30f;   // 2 pi / 128 - kStepHi
-  const float kf = rintf(phi * kInvStep);
-  float r = fmaf(-kf, kStepHi, phi);
-  r = fmaf(-kf, kStepLo, r);
-  const float2 cs = tab[static_cast<int>(kf) & (kTrigEntries - 1)];
-  const float r2 = r * r;
-  const float sr = fmaf(r * r2, fmaf(r2, 1.0f / 120.0f, -1.0f / 6.0f), r);
-  const float cr = fmaf(r2, fmaf(r2, 1.0f / 24.0f, -0.5f), 1.0f);
-  c = fmaf(cs.x, cr, -cs.y * sr);
-  s = fmaf(cs.y, cr, cs.x * sr);
+// cos and sin of an FP32 phase: Cody-Waite reduction by pi/2
+// (k = rint(phi * 2/pi); r = phi - k*C1 - k*C2 with C1 = fl(pi/2) and
+// C2 = fl(pi/2 - C1), each product exact inside the FMA), the hardware
+// sin/cos approximations on |r| <= pi/4 (__sincosf: absolute error below
+// 2^-21 on [-pi, pi]), then the quadrant k mod 4 swaps and negates. Within
+// 4e-7 of cos/sin(phi) for |phi| < 4e5 (k stays an exact FP32 integer),
+// far below the BF16 rounding of the output; calls with larger phases use
+// sincosf (MapTcParams::trig_exact). Few issue slots and no shared memory:
+// the epilogue warps share their schedulers with the MMA issuer.
+__device__ __forceinline__ void sincos_reduced(float phi, float& c, float& s) {
+  const float kTwoOverPi = 0x1.45f306p-1f;  // fl(2 / pi)
+  const float kC1 = 0x1.921fb6p+0f;         // fl(pi / 2)
+  const float kC2 = -0x1.777a5cp-25f;       // fl(pi / 2 - kC1)
+  const float kf = rintf(phi * kTwoOverPi);
+  float r = fmaf(-kf, kC1, phi);
+  r = fmaf(-kf, kC2, r);
+  float sr, cr;
+  __sincosf(r, &sr, &cr);
+  const int q = static_cast<int>(kf) & 3;
+  const float a = (q & 1) ? cr : sr;  // sin(phi) before the sign
+  const float b = (q & 1) ? sr : cr;  // cos(phi) before the sign
+  s = (q & 2) ? -a : a;
+  c = ((q + 1) & 2) ? -b : b;
 }
 
 // ------------------------------- producers ---------------------------------
@@ -142,7 +145,8 @@ __device__ __forceinline__ void sincos_tab(float phi, const float2* tab, float& 
 __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int lane) {
   const int NS = p.stages;
   const bool leader = pw == 0 && lane == 0;
-  int issued = 0;
+  int stage = 0;
+  uint32_t phase = 0;
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
@@ -164,9 +168,8 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
         valid = 0;
       }
       for (int j = 0; j < p.S; ++j) {
-        const int stage = issued % NS;
         // Warp-uniform outcome: the gather below uses full-warp shuffles.
-        const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), ((issued / NS) & 1) ^ 1, s.abort_flag, p.status);
+        const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), phase ^ 1u, s.abort_flag, p.status);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -200,7 +203,10 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
           cp_async_arrive_noinc(full);
           if (leader) mbar_arrive(full);
         }
-        ++issued;
+        if (++stage == NS) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
     }
   }
@@ -271,8 +277,16 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
   constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, kD);
   const uint64_t ones_desc = make_noswizzle_k16_desc(s.ones);
   const uint64_t bias_desc = make_noswizzle_k16_desc(s.bias);
+  // Descriptors of A stage 0 and weight slot 0: the start-address field holds
+  // address >> 4 in 14 bits and every shared address here is below 256 KB, so
+  // stage, slot and K-step offsets are plain additions of (bytes >> 4).
+  const uint64_t a_desc0 = make_sw128_kmajor_desc(s.a);
+  const uint64_t w_desc0 = make_sw128_kmajor_desc(s.w);
+  constexpr uint64_t kBlockDesc = kKBlockBytes >> 4;
   const int NS = p.stages;
-  int q = 0, wq = 0, n = 0, itc = 0;
+  int stage = 0;
+  uint32_t phase = 0;
+  int wq = 0, n = 0, itc = 0;
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
@@ -302,8 +316,7 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
             break;
           }
         }
-        const int stage = q % NS;
-        if (!mbar_wait(bar_at(s, kBarFull + stage), (q / NS) & 1, s.abort_flag, p.status)) {
+        if (!mbar_wait(bar_at(s, kBarFull + stage), phase, s.abort_flag, p.status)) {
           ok = false;
           break;
         }
@@ -311,19 +324,22 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
         // Value stages were written by cp.async (generic proxy); the MMA reads
         // them through the async proxy.
         if (it.kind == 1) fence_proxy_async_smem();
-        const uint32_t a0 = s.a + stage * kKBlockBytes;
-        const uint32_t b0 = s.w + wslot * kKBlockBytes;
+        const uint64_t ad = a_desc0 + stage * kBlockDesc;
+        const uint64_t bd = w_desc0 + wslot * kBlockDesc;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kPanelBytes + (kk & 3) * 32;
-          umma_bf16(d_tmem, make_sw128_kmajor_desc(a0 + off), make_sw128_kmajor_desc(b0 + off), idesc, 1u);
+          const uint64_t off = static_cast<uint64_t>((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
+          umma_bf16(d_tmem, ad + off, bd + off, idesc, 1u);
         }
         umma_commit(bar_at(s, kBarEmpty + stage));
+        if (++stage == NS) {
+          stage = 0;
+          phase ^= 1u;
+        }
         if (!p.w_resident) {
           umma_commit(bar_at(s, kBarWEmpty + wslot));
           ++wq;
         }
-        ++q;
       }
       if (!ok) break;
       umma_commit(bar_at(s, kBarAccFull + acc));
@@ -423,7 +439,7 @@ __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             float c, sn, o0, o1;
-            sincos_tab(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), s.trig, c, sn);
+            sincos_reduced(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), c, sn);
             rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
             ylo[e] = o0;
             yhi[e] = o1;
@@ -468,10 +484,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
   s.ones = s.bias + kBiasBlockBytes;
   const uint32_t e = s.ones + kOnesBytes;
   s.e_gen = base_gen + (e - base);
-  const uint32_t trig = e + kEpiWarps * kEpiWarpBytes;
-  float2* trig_gen = reinterpret_cast<float2*>(base_gen + (trig - base));
-  s.trig = trig_gen;
-  s.bars = trig + kTrigEntries * 8;
+  s.bars = e + kEpiWarps * kEpiWarpBytes;
   uint8_t* bars_gen = base_gen + (s.bars - base);
   s.tmem_holder = reinterpret_cast<uint32_t*>(bars_gen + 8 * kNumBars);
   s.abort_flag = reinterpret_cast<volatile int*>(bars_gen + 8 * kNumBars + 4);
@@ -504,7 +517,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
       const int kidx = ((idx >> 6) & 1) * 8 + (idx & 7);  // (byte/128 % 2) * 8 + byte%16/2
       ones[idx] = kidx < 2 ? static_cast<uint16_t>(0x3F80) : static_cast<uint16_t>(0);
     }
-    for (int idx = threadIdx.x; idx < kTrigEntries; idx += blockDim.x) trig_gen[idx] = p.trig[idx];
     fence_proxy_async_smem();
   }
   if (warp == kMmaWarp) {

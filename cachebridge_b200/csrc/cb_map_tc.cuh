@@ -22,7 +22,6 @@ constexpr int kTcThreads = 32 * (kLoaderWarp + 1);
 constexpr int kAccBufs = 4;                    // FP32 accumulators in TMEM (128 columns each)
 constexpr int kTmemCols = 128 * kAccBufs;      // all 512 TMEM columns
 constexpr int kEpiWarpBytes = 32 * 64;         // 32 token rows x 64 B staging per epilogue warp
-constexpr int kTrigEntries = 128;              // (cos, sin)(2*pi*k/128) table
 constexpr int kTcMaxSmem = 232448;             // sm_100 opt-in dynamic shared memory per block
 
 struct MapTcParams {
@@ -61,8 +60,7 @@ struct MapTcParams {
   float dst_inv_freq[64];   // target RoPE
   float dst_magnitude;
   int64_t position_start;   // absolute position of token 0
-  int trig_exact;           // 1 when a phase can exceed the table method's range: use sincosf
-  float2 trig[kTrigEntries];  // (cos, sin)(2*pi*k/128), rounded to FP32 from double
+  int trig_exact;           // 1 when a phase can exceed the reduced method's range: use sincosf
   int32_t* status;
   // 4-D map of the key workspace {128, H, n_tokens, U}, box {64, 1, 128, 1},
   // 128B-swizzled, so a box lands in the UMMA K-major SW128 layout.
@@ -73,7 +71,7 @@ __global__ void map_install_tc_kernel(const __grid_constant__ MapTcParams p);
 
 // Shared memory bytes of everything but the weight slots and A stages.
 constexpr int kTcFixedSmem = 1024 /* alignment slack */ + kBiasBlockBytes + kOnesBytes +
-                             kEpiWarps * kEpiWarpBytes + kTrigEntries * 8 + 512 /* barriers */;
+                             kEpiWarps * kEpiWarpBytes + 512 /* barriers */;
 
 // Shared-memory bytes the kernel needs for a given weight-slot / stage split.
 inline int tc_smem_bytes(int w_slots, int stages) {

@@ -355,3 +355,59 @@ def test_padded_destination_rows(tmp_path, cuda_device):
         assert bool((got[:, mask].float() == CANARY).all()), "an untouched row changed"
         pad = flat[kind, :, 8:].reshape(L_t, rows, stride)[:, :, H * D :]
         assert bool((pad.float() == CANARY).all()) and bool((flat[kind, :, :8].float() == CANARY).all())
+
+
+@pytest.mark.parametrize("start", [0, 389_000, 600_000])
+def test_target_rope_at_far_positions(tmp_path, cuda_device, start):
+    """Target RoPE in the tensor-core epilogue: phases below 4e5 rad take the
+    reduced hardware sin/cos, larger ones sincosf; both against the oracle."""
+    g = torch.Generator().manual_seed(77 + start)
+    L_s, L_t, H, D, S, n = 6, 3, 2, 128, 2, 200
+    mapper_dir = _random_mapper(tmp_path, seed=31, L_s=L_s, L_t=L_t, H=H, D=D, S=S)
+    positions = torch.arange(start, start + n)
+    src_slots = torch.randperm(400, generator=g)[:n]
+    dst_slots = torch.randperm(400, generator=g)[:n]
+    src_pool, page = _content_pool(g, layers=L_s, rows=400, heads=H, D=D, dtype=torch.bfloat16, theta=1e6,
+                                   positions=positions, slots=src_slots, device=cuda_device)
+    dst_pool = TokenKVPool(layers=L_t, rows=400, heads=H, head_dim=D, device=cuda_device, fill=CANARY)
+    mapper = PageMapper(mapper_dir, method="cachebridge", source_rope_theta=1e6, target_rope_theta=1e6,
+                        device=cuda_device)
+    mapper.map_install(src_pool.rows(src_slots.to(cuda_device)), dst_pool.rows(dst_slots.to(cuda_device)), n, start)
+    torch.cuda.synchronize()
+    raise_for_status(cuda_device)
+    layers, head_range = orc.load_layers(mapper_dir)
+    f32 = orc.map_page_f32(layers, page, head_range=head_range, position_start=start, source_theta=1e6,
+                           target_theta=1e6)
+    _check_install(dst_pool, dst_slots, f32, dtype=torch.bfloat16)
+
+
+def test_config2_full_size_properties(tmp_path, cuda_device):
+    """BASELINE config 2 shapes at the full 8192-token history: every target
+    row lands at its slot and nothing else changes (bit-exact), and a token
+    window of every layer and head matches the oracle within the BF16 bound."""
+    g = torch.Generator().manual_seed(2024)
+    L_s, L_t, H, D, S, n, rows = 40, 64, 8, 128, 2, 8192, 12288
+    mapper_dir = _random_mapper(tmp_path, seed=77, L_s=L_s, L_t=L_t, H=H, D=D, S=S)
+    src_slots = torch.randperm(rows, generator=g)[:n]
+    dst_slots = torch.randperm(rows, generator=g)[:n]
+    positions = torch.arange(n)
+    src_pool, page = _content_pool(g, layers=L_s, rows=rows, heads=H, D=D, dtype=torch.bfloat16, theta=1e6,
+                                   positions=positions, slots=src_slots, device=cuda_device)
+    dst_pool = TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=cuda_device, fill=CANARY)
+    mapper = PageMapper(mapper_dir, method="cachebridge", source_rope_theta=1e6, target_rope_theta=1e6,
+                        device=cuda_device)
+    mapper.map_install(src_pool.rows(src_slots.to(cuda_device)), dst_pool.rows(dst_slots.to(cuda_device)), n, 0)
+    torch.cuda.synchronize()
+    raise_for_status(cuda_device)
+    untouched = torch.ones(rows, dtype=torch.bool, device=cuda_device)
+    untouched[dst_slots.to(cuda_device)] = False
+    for buf in (dst_pool.k_buffer, dst_pool.v_buffer):
+        assert bool((buf[:, untouched].float() == CANARY).all()), "an untouched row changed"
+        assert not bool((buf[:, ~untouched].float() == CANARY).all(dim=-1).any()), "a target row was not written"
+    a, b = 5000, 5256  # a window away from the start (large phases, several m-tiles in)
+    layers, head_range = orc.load_layers(mapper_dir)
+    f32 = orc.map_page_f32(layers, page[:, :, a:b].contiguous(), head_range=head_range, position_start=a,
+                           source_theta=1e6, target_theta=1e6)
+    loc = dst_slots[a:b].to(cuda_device)
+    got = torch.stack([dst_pool.k_buffer[:, loc], dst_pool.v_buffer[:, loc]])
+    check_bf16(got, f32)
