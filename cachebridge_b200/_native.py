@@ -123,14 +123,14 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_rope_table.argtypes = [c_vp, rope_p, c_i64, c_i64, c_vp, c_vp, c_i64]
     lib.cb_map_install.restype = c_int
     lib.cb_map_install.argtypes = [
-        c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp, c_size, c_vp
+        c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp, c_size, c_vp, c_vp
     ]
     lib.cb_map_install_noalloc.restype = c_int
     lib.cb_map_install_noalloc.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, rope_p, c_int, c_vp]
     lib.cb_derotate_keys.restype = c_int
-    lib.cb_derotate_keys.argtypes = [c_vp, c_vp, rows_p, c_i64, c_i64, rope_p, c_vp, c_size, c_vp]
+    lib.cb_derotate_keys.argtypes = [c_vp, c_vp, rows_p, c_i64, c_i64, rope_p, c_vp, c_size, c_vp, c_vp]
     lib.cb_map_install_packed.restype = c_int
-    lib.cb_map_install_packed.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, c_vp, c_size, c_vp]
+    lib.cb_map_install_packed.argtypes = [c_vp, c_vp, rows_p, rows_p, c_i64, c_i64, rope_p, c_vp, c_size, c_vp, c_vp]
     lib.cb_pack_rows.restype = c_int
     lib.cb_pack_rows.argtypes = [c_vp, rows_p, c_int, c_int, c_i64, c_vp, c_vp]
     lib.cb_install_rows.restype = c_int

@@ -208,7 +208,8 @@ int launch_rope_table(cudaStream_t st, const cb_rope* rope, int64_t position_sta
                       float* out_sin, int64_t out_stride);
 
 int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int64_t n_tokens,
-                    int64_t position_start, const cb_rope* src_rope, void* workspace, int32_t* dev_status) {
+                    int64_t position_start, const cb_rope* src_rope, void* workspace, const int32_t* order,
+                    int32_t* dev_status) {
   cbk::DerotateParams dp{};
   dp.n_tokens = n_tokens;
   dp.H = m->H;
@@ -222,6 +223,7 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
   dp.src_slots = src->slots;
   dp.rope = rope_dev(src_rope);
   dp.position_start = position_start;
+  dp.order = order;
   dp.ws = static_cast<__nv_bfloat16*>(workspace);
   dp.status = dev_status;
   const int blocks = static_cast<int>((n_tokens + 7) / 8);
@@ -256,7 +258,7 @@ int tc_chunk_mtiles(int64_t n_tokens, int64_t groups, int grid) {
 
 int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst,
               int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope, const void* workspace,
-              int32_t* dev_status) {
+              const int32_t* order, int32_t* dev_status) {
   cbk::MapTcParams p{};
   p.n_tokens = static_cast<int>(n_tokens);
   p.L_t = m->L_t;
@@ -307,6 +309,7 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   std::memcpy(p.dst_inv_freq, dst_rope->inv_freq, sizeof(p.dst_inv_freq));
   p.dst_magnitude = dst_rope->magnitude;
   p.position_start = position_start;
+  p.order = order;
   {
     float max_inv = 0.f;
     for (int i = 0; i < dst_rope->half_dim; ++i) max_inv = std::max(max_inv, std::fabs(dst_rope->inv_freq[i]));
@@ -551,7 +554,7 @@ int cb_rope_table(void* stream, const cb_rope* rope, int64_t position_start, int
 int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
                    int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
                    const cb_rope* dst_rope, int dtype, void* workspace, size_t workspace_bytes,
-                   int32_t* dev_status) {
+                   const int32_t* token_order, int32_t* dev_status) {
   if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
   if (dtype != CB_DTYPE_BF16 && dtype != CB_DTYPE_F32) return fail(CB_ERR_UNSUPPORTED, "dtype must be bf16 or fp32");
   if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
@@ -574,9 +577,10 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
 
   if (tc) {
     if ((rc = check_tc_extras(m, dtype, n_tokens, workspace, workspace_bytes)) != CB_OK) return rc;
-    if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, workspace, dev_status)) != CB_OK)
+    if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, workspace, token_order,
+                              dev_status)) != CB_OK)
       return rc;
-    return launch_tc(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, dev_status);
+    return launch_tc(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, token_order, dev_status);
   }
 
   // Generic CUDA-core path.
@@ -621,7 +625,8 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
 
 int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_tokens,
                      int64_t position_start, const cb_rope* src_rope, void* workspace,
-                     size_t workspace_bytes, int32_t* dev_status) {
+                     size_t workspace_bytes, const int32_t* token_order,
+                     int32_t* dev_status) {
   int rc = check_tc_call(m, src, nullptr, n_tokens);
   if (rc != CB_OK) return rc;
   if ((rc = check_rope(src_rope, m->D, "source RoPE")) != CB_OK) return rc;
@@ -632,12 +637,14 @@ int cb_derotate_keys(cb_mapper* m, void* stream, const cb_rows* src, int64_t n_t
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
   if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
   return launch_derotate(m, static_cast<cudaStream_t>(stream), src, n_tokens, position_start, src_rope, workspace,
+                         token_order,
                          dev_status);
 }
 
 int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows* dst,
                           int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope,
-                          const void* workspace, size_t workspace_bytes, int32_t* dev_status) {
+                          const void* workspace, size_t workspace_bytes,
+                          const int32_t* token_order, int32_t* dev_status) {
   int rc = check_tc_call(m, src, dst, n_tokens);
   if (rc != CB_OK) return rc;
   if ((rc = check_rope(dst_rope, m->D, "target RoPE")) != CB_OK) return rc;
@@ -649,6 +656,7 @@ int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const 
   if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
   if ((rc = ensure_rows_access(m->device, dst, "dst rows")) != CB_OK) return rc;
   return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, position_start, dst_rope, workspace,
+                   token_order,
                    dev_status);
 }
 
@@ -913,7 +921,7 @@ int cb_map_install_noalloc(cb_mapper* m, void* stream, const cb_rows* src, const
     if (rc != CB_OK) return rc;
   }
   return cb_map_install(m, stream, src, dst, n_tokens, position_start, src_rope, dst_rope, dtype, scratch,
-                        static_cast<size_t>(CB_NOALLOC_SCRATCH_BYTES), dev_status);
+                        static_cast<size_t>(CB_NOALLOC_SCRATCH_BYTES), nullptr, dev_status);
 }
 
 }  // extern "C"

@@ -57,6 +57,19 @@ __device__ __forceinline__ void flag_error(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(reinterpret_cast<int*>(status), bits);
 }
 
+// Token handled at processing index i of a call: token_order[i] when the
+// caller gave an order (a permutation of [0, n)), else i. An entry outside
+// [0, n) flags CB_DEV_ERR_SLOT_RANGE and returns -1 (the row is skipped).
+__device__ __forceinline__ int token_at(const int32_t* order, int i, int n, int32_t* status) {
+  if (order == nullptr) return i;
+  const int t = __ldg(order + i);
+  if (t < 0 || t >= n) {
+    flag_error(status, CB_DEV_ERR_SLOT_RANGE);
+    return -1;
+  }
+  return t;
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory addressing, fences, timers
 // ---------------------------------------------------------------------------

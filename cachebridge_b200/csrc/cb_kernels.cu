@@ -56,14 +56,16 @@ __global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_cons
   const int g = lane >> 3;
   const int j = lane & 7;
 
-  int64_t slot = load_slot(p.src_slots, p.src_slot_dtype, t);
-  if (slot < 0 || slot >= p.src_rows) {
+  // Processing index t holds token `tok` (the caller's order, or t itself).
+  const int tok = token_at(p.order, static_cast<int>(t), static_cast<int>(p.n_tokens), lane == 0 ? p.status : nullptr);
+  int64_t slot = tok < 0 ? -1 : load_slot(p.src_slots, p.src_slot_dtype, tok);
+  if (tok >= 0 && (slot < 0 || slot >= p.src_rows)) {
     if (lane == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
     slot = -1;
   }
   float c[8], s[8];
   {
-    const float pos = static_cast<float>(p.position_start + t);
+    const float pos = static_cast<float>(p.position_start + (tok < 0 ? 0 : tok));
 #pragma unroll
     for (int e = 0; e < 8; ++e) rope_coeff(pos, p.rope.inv_freq[8 * j + e], p.rope.magnitude, c[e], s[e]);
 #pragma unroll

@@ -29,7 +29,8 @@ struct DerotateParams {
   const void* src_slots;
   RopeDev rope;  // source RoPE
   int64_t position_start;
-  __nv_bfloat16* ws;  // [U][n][H][128]
+  const int32_t* order;  // processing order of the tokens, or null
+  __nv_bfloat16* ws;  // [U][n][H][128], rows in processing order
   int32_t* status;
 };
 

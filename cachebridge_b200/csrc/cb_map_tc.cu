@@ -150,18 +150,29 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    // Slot of this lane's token row, prefetched one m-tile ahead (values only).
+    // Source slot of this lane's row (processing index next_t holds token
+    // p.order[next_t]), prefetched one m-tile ahead (values only).
     int next_t = it.tok0 + pw * 32 + lane;
-    int next_valid = next_t < p.n_tokens;
-    int64_t next_row = next_valid && it.kind == 1 ? load_slot(p.src_slots, p.src_slot_dtype, next_t) : 0;
+    int next_valid = 0;
+    int64_t next_row = 0;
+    if (it.kind == 1 && next_t < p.n_tokens) {
+      const int tok = token_at(p.order, next_t, p.n_tokens, p.status);
+      next_valid = tok >= 0;
+      if (next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, tok);
+    }
     for (int m = 0; m < it.mtiles && ok; ++m) {
       const int tok0 = it.tok0 + m * kBM;
       int valid = next_valid;
       int64_t srow = next_row;
       if (m + 1 < it.mtiles) {
         next_t += kBM;
-        next_valid = next_t < p.n_tokens;
-        next_row = next_valid && it.kind == 1 ? load_slot(p.src_slots, p.src_slot_dtype, next_t) : 0;
+        next_valid = 0;
+        next_row = 0;
+        if (it.kind == 1 && next_t < p.n_tokens) {
+          const int tok = token_at(p.order, next_t, p.n_tokens, p.status);
+          next_valid = tok >= 0;
+          if (next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, tok);
+        }
       }
       if (it.kind == 1 && valid && (srow < 0 || srow >= p.src_rows)) {
         flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
@@ -392,15 +403,17 @@ __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_
       const uint32_t tbase = lane_base + acc * kD;
       const int t = it.tok0 + m * kBM + eq * 32 + lane;
       char* row_ptr = nullptr;  // this lane's destination row, or null
-      if (t < p.n_tokens) {
-        const int64_t slot = load_slot(p.dst_slots, p.dst_slot_dtype, t);
+      int tok = -1;  // the token at processing index t
+      if (t < p.n_tokens) tok = token_at(p.order, t, p.n_tokens, p.status);
+      if (tok >= 0) {
+        const int64_t slot = load_slot(p.dst_slots, p.dst_slot_dtype, tok);
         if (slot < 0 || slot >= p.dst_rows)
           flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
         else
           row_ptr = dst_layer + slot * dst_stride_bytes;
       }
       const bool do_rope = it.kind == 0 && row_ptr != nullptr;
-      const float pos = static_cast<float>(p.position_start + t);
+      const float pos = static_cast<float>(p.position_start + (tok < 0 ? 0 : tok));
       // Warp-uniform outcome: tcgen05.ld is .sync.aligned across the warp.
       const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (n >> 2) & 1, s.abort_flag, p.status);
       if (!__all_sync(0xffffffffu, got)) {

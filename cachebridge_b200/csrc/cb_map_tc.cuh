@@ -41,7 +41,7 @@ struct MapTcParams {
   const int* sel_global;    // [L_t][S] source layer ids
   const int* sel_local;     // [L_t][S] index into the workspace's used-layer list
 
-  const __nv_bfloat16* ws_k;  // [U][n_tokens][H][128] content-space keys
+  const __nv_bfloat16* ws_k;  // [U][n_tokens][H][128] content-space keys, processing order
   const void* src_v[CB_MAX_LAYERS];
   int64_t src_row_stride;   // elements
   int64_t src_rows;
@@ -60,6 +60,7 @@ struct MapTcParams {
   float dst_inv_freq[64];   // target RoPE
   float dst_magnitude;
   int64_t position_start;   // absolute position of token 0
+  const int32_t* order;     // token at each processing index (null: identity)
   int trig_exact;           // 1 when a phase can exceed the reduced method's range: use sincosf
   int32_t* status;
   // 4-D map of the key workspace {128, H, n_tokens, U}, box {64, 1, 128, 1},

@@ -164,6 +164,12 @@ CB_API int cb_rope_table(void* stream, const cb_rope* rope, int64_t position_sta
  *        209-214).
  *   dtype: storage dtype of src and dst rows (CB_DTYPE_BF16 or CB_DTYPE_F32).
  *   workspace: >= cb_mapper_workspace_bytes(mapper, dtype, n_tokens) bytes.
+ *   token_order: NULL, or a device int32 array [n_tokens] holding a
+ *        permutation of 0..n_tokens-1: the order in which the tensor-core path
+ *        processes the tokens (128 per tile). Results do not depend on it.
+ *        An order that sorts dst->slots makes each tile's stores land in a few
+ *        memory pages. Entries outside [0, n_tokens) are skipped and flag
+ *        CB_DEV_ERR_SLOT_RANGE.
  *   dev_status: device int32 status word (CB_DEV_ERR_* bits are OR-ed in).
  * Compute: keys have the source RoPE removed in FP32, features of the S
  * selected source layers are concatenated, y = x W + b is accumulated in FP32,
@@ -174,7 +180,7 @@ CB_API int cb_rope_table(void* stream, const cb_rope* rope, int64_t position_sta
 CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
                    const cb_rows* dst, int64_t n_tokens, int64_t position_start,
                    const cb_rope* src_rope, const cb_rope* dst_rope, int dtype, void* workspace,
-                   size_t workspace_bytes, int32_t* dev_status);
+                   size_t workspace_bytes, const int32_t* token_order, int32_t* dev_status);
 
 /*
  * cb_map_install without a caller workspace; no counterpart in the reference.
@@ -193,7 +199,7 @@ CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
  * calls whose GPU work can overlap (streams not ordered with one another,
  * concurrent host threads) race on it and must be serialised by the caller.
  * Nothing in the array needs to start at zero. Arguments and results are
- * those of cb_map_install.
+ * those of cb_map_install with token_order NULL.
  */
 #define CB_NOALLOC_SCRATCH_BYTES (64 << 20)
 CB_API int cb_map_install_noalloc(cb_mapper* mapper, void* stream, const cb_rows* src,
@@ -212,15 +218,17 @@ CB_API int cb_map_install_noalloc(cb_mapper* mapper, void* stream, const cb_rows
  *  cb_map_install_packed: map keys from `workspace` and values from the
  *    source rows, add the bias, apply the target RoPE and install into dst rows.
  * cb_map_install(...) == cb_derotate_keys(...) then cb_map_install_packed(...)
- * on the same stream, with the same workspace and position_start.
+ * on the same stream, with the same workspace, position_start and token_order
+ * (the workspace holds the keys in processing order).
  */
 CB_API int cb_derotate_keys(cb_mapper* mapper, void* stream, const cb_rows* src,
                      int64_t n_tokens, int64_t position_start, const cb_rope* src_rope,
-                     void* workspace, size_t workspace_bytes, int32_t* dev_status);
+                     void* workspace, size_t workspace_bytes, const int32_t* token_order,
+                     int32_t* dev_status);
 CB_API int cb_map_install_packed(cb_mapper* mapper, void* stream, const cb_rows* src,
                           const cb_rows* dst, int64_t n_tokens, int64_t position_start,
                           const cb_rope* dst_rope, const void* workspace,
-                          size_t workspace_bytes, int32_t* dev_status);
+                          size_t workspace_bytes, const int32_t* token_order, int32_t* dev_status);
 
 /*
  * Row gather: out[kind][l][t][:] = src.{k,v}[l][src.slots[t]][row] for all

@@ -46,7 +46,7 @@ def test_argument_validation_without_gpu():
     rc = lib.cb_rope_table(None, ctypes.byref(rope), 0, 4, None, None, 4)
     assert rc == nat.CB_ERR_INVALID
     assert b"rope table" in lib.cb_last_error()
-    rc = lib.cb_map_install(None, None, None, None, 0, 0, None, None, 1, None, 0, None)
+    rc = lib.cb_map_install(None, None, None, None, 0, 0, None, None, 1, None, 0, None, None)
     assert rc == nat.CB_ERR_INVALID
     out = ctypes.c_void_p()
     rc = lib.cb_mapper_create(ctypes.byref(out), 0, 0, 1, 128, 1, None, None, None, None, None)
