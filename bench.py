@@ -182,6 +182,61 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------
+# Re-prefill estimate (what the handoff saves)
+# ----------------------------------------------------------------------------
+QWEN32B = dict(layers=64, hidden=5120, q_heads=64, kv_heads=8, head_dim=128, mlp=25600)
+
+
+def reprefill_estimate(device, *, tokens, requests, tp, reps=3):
+    """Time one Qwen3-32B-shaped decoder layer's prefill over ``tokens`` on
+    this rank's tensor-parallel shard (bf16 torch.matmul for QKV, output and
+    the gated MLP; causal SDPA with grouped KV heads; random weights), then
+    scale to all layers and ``requests`` requests. Norms, RoPE and the two
+    per-layer TP all-reduces are left out, so the estimate is a lower bound
+    on the real re-prefill time."""
+    import torch.nn.functional as F
+
+    c = QWEN32B
+    nq, nkv, d = c["q_heads"] // tp, c["kv_heads"] // tp, c["head_dim"]
+    inter = c["mlp"] // tp
+    g = torch.Generator(device=device).manual_seed(123)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    wqkv, wo = w(c["hidden"], (nq + 2 * nkv) * d), w(nq * d, c["hidden"])
+    wgu, wdown = w(c["hidden"], 2 * inter), w(inter, c["hidden"])
+    x = w(tokens, c["hidden"])
+
+    def layer(x):
+        qkv = x @ wqkv
+        q, k, v = qkv.split([nq * d, nkv * d, nkv * d], dim=-1)
+        q = q.view(tokens, nq, d).transpose(0, 1)[None]
+        k = k.view(tokens, nkv, d).transpose(0, 1)[None]
+        v = v.view(tokens, nkv, d).transpose(0, 1)[None]
+        att = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        h = x + att[0].transpose(0, 1).reshape(tokens, nq * d) @ wo
+        gate, up = (h @ wgu).chunk(2, dim=-1)
+        return h + (F.silu(gate) * up) @ wdown
+
+    with torch.inference_mode():
+        for _ in range(2):
+            layer(x)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        a.record()
+        for _ in range(reps):
+            layer(x)
+        b.record()
+        b.synchronize()
+    per_layer = a.elapsed_time(b) / reps
+    return dict(ms=per_layer * c["layers"] * requests, per_layer_ms=per_layer, tokens_per_request=tokens,
+                requests=requests, layers=c["layers"], tp=tp,
+                model="Qwen3-32B-shaped proxy: hidden 5120, 64 q / 8 kv heads, head_dim 128, MLP 25600, "
+                      "random bf16 weights; norms, RoPE and TP all-reduces omitted (lower bound)")
+
+
+# ----------------------------------------------------------------------------
 # CPU reference (oracle restatement of the reference's torch CPU path)
 # ----------------------------------------------------------------------------
 def cpu_reference_tokens_per_s(layers, *, n_sample, reps, seed=7):
@@ -356,6 +411,11 @@ def run_single(args):
     h2d = block_host.numel() * 2 + idx_host.numel() * 8
     del block_dev, block_host
 
+    # ---- re-prefill estimate of the same history on this GPU ---------------------
+    prefill = reprefill_estimate(dev, tokens=n, requests=1, tp=1)
+    prefill["handoff_ms"] = statistics.median(step_ms)
+    prefill["handoff_faster"] = prefill["handoff_ms"] < prefill["ms"]
+
     # ---- CPU baseline (reference algorithm on host cores, bounded sample) -------
     cpu_value, cores = cpu_reference_tokens_per_s(layers, n_sample=args.cpu_tokens, reps=2)
 
@@ -390,6 +450,7 @@ def run_single(args):
                  latency_p50_ms=1e3 * statistics.median(e2e_times)),
         gpu_launches=launches_per_step * args.steps,
         clocks=clocks.summary(),
+        reprefill_estimate=prefill,
     )
     print(json.dumps(line), flush=True)
     return 0
@@ -533,6 +594,15 @@ def run_sharded(args):
     if int(vote_host.item()) != 1:
         raise RuntimeError("end-to-end handoff was not published")
 
+    # Re-prefill estimate on the target TP group (every rank runs its shard; max over ranks).
+    prefill = reprefill_estimate(dev, tokens=n_tok, requests=n_req, tp=plan.tp)
+    prefill_ms = torch.tensor([prefill["per_layer_ms"]], device=dev)
+    dist.all_reduce(prefill_ms, op=dist.ReduceOp.MAX)
+    prefill["per_layer_ms"] = float(prefill_ms)
+    prefill["ms"] = prefill["per_layer_ms"] * prefill["layers"] * n_req
+    prefill["handoff_ms"] = total_ms / args.steps
+    prefill["handoff_faster"] = prefill["handoff_ms"] < prefill["ms"]
+
     launches = torch.tensor([runner.launches * args.steps if runner is not None else 0], device=dev)
     dist.all_reduce(launches)
     clk = clocks.summary()
@@ -571,6 +641,7 @@ def run_sharded(args):
                      ms_per_step=float(e2e_ms)),
             gpu_launches=int(launches.item()),
             clocks=clk,
+            reprefill_estimate=prefill,
         )
         print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
