@@ -303,7 +303,9 @@ def run_reference(args):
         impl="reference", metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps,
         warmup=args.warmup, ms_per_step=1e3 * elapsed / args.steps, higher_is_better=True,
         scaling="weak" if args.gpus == 1 else "strong", vs_baseline=None, dtype="f32", data="synthetic",
-        config=dict(workload="qwen3-14b->32b handoff (BASELINE config 2), CPU sample", tokens_per_step=n_sample,
+        config=dict(workload=("qwen3-14b->32b single-GPU handoff (BASELINE config 2)" if args.gpus == 1 else
+                              f"qwen3-14b->32b sharded handoff (BASELINE config 3), TP{args.gpus // 2}+TP{args.gpus // 2}")
+                    + ", reference algorithm on host CPU, bounded sample", tokens_per_step=n_sample,
                     source_layers=L_s, target_layers=QWEN["L_t"], kv_heads=H, head_dim=D, selected=QWEN["S"]),
         cpu_baseline=dict(value=value, unit=UNIT, cores=cores, kind="port",
                           sample=f"{n_sample} of the 8192 history tokens per step (one reference block), "
