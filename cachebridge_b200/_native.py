@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "cb_status_string",
     "cb_last_error",
     "cb_mapper_create",
+    "cb_mapper_create_dense",
     "cb_mapper_destroy",
     "cb_mapper_info",
     "cb_mapper_workspace_bytes",
@@ -112,6 +113,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_mapper_create.restype = c_int
     lib.cb_mapper_create.argtypes = [
         ctypes.POINTER(c_vp), c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp
+    ]
+    lib.cb_mapper_create_dense.restype = c_int
+    lib.cb_mapper_create_dense.argtypes = [
+        ctypes.POINTER(c_vp), c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp
     ]
     lib.cb_mapper_destroy.restype = c_int
     lib.cb_mapper_destroy.argtypes = [c_vp]

@@ -183,6 +183,10 @@ cbk::RopeDev rope_dev(const cb_rope* r) {
 struct cb_mapper {
   int device = 0;
   int L_t = 0, H = 0, D = 0, S = 0, U = 0;
+  // Dense (nv_transfer) mappers read every source head: Hs source heads per
+  // selected layer feed each target head, so a unit has KB = S * Hs k-blocks.
+  // Headwise mappers: Hs = 0 (target head h reads source head h), KB = S.
+  int Hs = 0, KB = 0;
   int num_sms = 0;
   int max_sel = 0;
   std::vector<int> used;  // sorted unique selected source layers
@@ -196,12 +200,18 @@ struct cb_mapper {
 
 namespace {
 
+int mapper_create(cb_mapper** out, int device, int target_layers, int heads, int head_dim, int num_selected,
+                  const int64_t* selected, const float* k_weight, const float* k_bias, const float* v_weight,
+                  const float* v_bias, int src_heads);
 int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
                     size_t workspace_bytes);
 
-// Tensor-core workspace: BF16 content-space keys [U][n][H][128].
+// Source heads a call reads per source layer (all of them for a dense mapper).
+int ws_heads(const cb_mapper* m) { return m->Hs > 0 ? m->Hs : m->H; }
+
+// Tensor-core workspace: BF16 content-space keys [U][n][ws_heads][128].
 size_t ws_total_bytes(const cb_mapper* m, int64_t n) {
-  return static_cast<size_t>(m->U) * static_cast<size_t>(n) * m->H * cbk::kD * 2;
+  return static_cast<size_t>(m->U) * static_cast<size_t>(n) * ws_heads(m) * cbk::kD * 2;
 }
 
 int launch_rope_table(cudaStream_t st, const cb_rope* rope, int64_t position_start, int64_t n, float* out_cos,
@@ -212,7 +222,7 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
                     int32_t* dev_status) {
   cbk::DerotateParams dp{};
   dp.n_tokens = n_tokens;
-  dp.H = m->H;
+  dp.H = ws_heads(m);
   dp.U = m->U;
   for (int l = 0; l < src->layers; ++l) dp.src_k[l] = src->k[l];
   dp.used = m->used_dev;
@@ -264,6 +274,10 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.L_t = m->L_t;
   p.H = m->H;
   p.S = m->S;
+  p.KB = m->KB;
+  p.kb_heads = m->Hs > 0 ? m->Hs : 1;
+  p.dense = m->Hs > 0 ? 1 : 0;
+  p.ws_heads = ws_heads(m);
   p.R = tc_chunk_mtiles(n_tokens, 2ll * m->H * m->L_t, m->num_sms);
   p.n_chunks = static_cast<int>((n_tokens + p.R * cbk::kBM - 1) / (p.R * cbk::kBM));
   const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
@@ -271,14 +285,14 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.num_items = static_cast<int>(items);
   // Weights stay resident for a whole item when they leave room for >= 2 A
   // stages; otherwise two weight slots are streamed per m-tile.
-  const int res_stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(m->S, 0)) / cbk::kKBlockBytes;
-  p.w_resident = (m->S <= 4 && res_stages >= 2) ? 1 : 0;
-  p.w_slots = p.w_resident ? m->S : 2;
+  const int res_stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(m->KB, 0)) / cbk::kKBlockBytes;
+  p.w_resident = (m->KB <= 4 && res_stages >= 2) ? 1 : 0;
+  p.w_slots = p.w_resident ? m->KB : 2;
   const int stages = (cbk::kTcMaxSmem - cbk::tc_smem_bytes(p.w_slots, 0)) / cbk::kKBlockBytes;
   p.stages = std::min(stages, 4);
   if (p.stages < 2) return fail(CB_ERR_UNSUPPORTED, "shared memory too small for the pipeline");
   p.w_img = m->w_img;
-  p.unit_bytes = static_cast<int64_t>(m->S) * cbk::kKBlockBytes + cbk::kBiasBlockBytes;
+  p.unit_bytes = static_cast<int64_t>(m->KB) * cbk::kKBlockBytes + cbk::kBiasBlockBytes;
   p.sel_global = m->sel;
   p.sel_local = m->sel_local;
   p.ws_k = static_cast<const __nv_bfloat16*>(workspace);
@@ -286,10 +300,10 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.src_row_stride = src->row_stride;
   p.src_rows = src->rows;
   {
-    const cuuint64_t kdims[4] = {128, static_cast<cuuint64_t>(m->H), static_cast<cuuint64_t>(n_tokens),
+    const cuuint64_t kdims[4] = {128, static_cast<cuuint64_t>(ws_heads(m)), static_cast<cuuint64_t>(n_tokens),
                                  static_cast<cuuint64_t>(m->U)};
-    const cuuint64_t kstr[3] = {256, static_cast<cuuint64_t>(m->H) * 256,
-                                static_cast<cuuint64_t>(n_tokens) * m->H * 256};
+    const cuuint64_t kstr[3] = {256, static_cast<cuuint64_t>(ws_heads(m)) * 256,
+                                static_cast<cuuint64_t>(n_tokens) * ws_heads(m) * 256};
     const cuuint32_t kbox[4] = {64, 1, 128, 1};
     int rc = encode_bf16_map(&p.kmap, 4, workspace, kdims, kstr, kbox);
     if (rc != CB_OK) return rc;
@@ -345,7 +359,7 @@ int check_tc_call(const cb_mapper* m, const cb_rows* src, const cb_rows* dst, in
   if (m == nullptr) return fail(CB_ERR_INVALID, "null mapper");
   if (n_tokens < 0) return fail(CB_ERR_INVALID, "negative token count");
   if (n_tokens > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "too many tokens in one call");
-  int rc = check_rows(src, "src", m->D, m->H, CB_DTYPE_BF16, true);
+  int rc = check_rows(src, "src", m->D, ws_heads(m), CB_DTYPE_BF16, true);
   if (rc != CB_OK) return rc;
   if (src->layers <= m->max_sel) return fail(CB_ERR_INVALID, "mapper selected layer exceeds source page depth");
   if (dst != nullptr) {
@@ -394,6 +408,47 @@ const char* cb_last_error(void) { return g_last_error.c_str(); }
 int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, int head_dim,
                      int num_selected, const int64_t* selected, const float* k_weight,
                      const float* k_bias, const float* v_weight, const float* v_bias) {
+  return mapper_create(out, device, target_layers, heads, head_dim, num_selected, selected, k_weight, k_bias,
+                       v_weight, v_bias, 0);
+}
+
+int cb_mapper_create_dense(cb_mapper** out, int device, int target_layers, int target_heads, int source_heads,
+                           int head_dim, int num_selected, const int64_t* selected, const float* k_weight,
+                           const float* k_bias, const float* v_weight, const float* v_bias) {
+  if (out == nullptr) return fail(CB_ERR_INVALID, "null output handle");
+  *out = nullptr;
+  if (head_dim != cbk::kD) return fail(CB_ERR_UNSUPPORTED, "dense (nv_transfer) mappers need head_dim 128");
+  if (source_heads <= 0 || target_heads <= 0 || num_selected <= 0 || target_layers <= 0)
+    return fail(CB_ERR_INVALID, "dense mapper: counts must be positive");
+  if (static_cast<int64_t>(num_selected) * source_heads > 64)
+    return fail(CB_ERR_UNSUPPORTED, "dense mapper: at most 64 (selected layer, source head) feature blocks");
+  if (!k_weight || !v_weight) return fail(CB_ERR_INVALID, "null mapper tensor");
+  // [L_t][F][H][D] (F = S * Hs * D, the reference's k_weight[:, head_slice]) ->
+  // [L_t][H][F][D]: per target head, the same shape as a headwise map.
+  const int64_t F = static_cast<int64_t>(num_selected) * source_heads * head_dim;
+  const size_t per_layer = static_cast<size_t>(F) * target_heads * head_dim;
+  std::vector<float> kw(per_layer * target_layers), vw(per_layer * target_layers);
+  for (int l = 0; l < target_layers; ++l)
+    for (int64_t f = 0; f < F; ++f)
+      for (int h = 0; h < target_heads; ++h) {
+        const size_t from = l * per_layer + (static_cast<size_t>(f) * target_heads + h) * head_dim;
+        const size_t to = l * per_layer + (static_cast<size_t>(h) * F + f) * head_dim;
+        std::memcpy(&kw[to], k_weight + from, head_dim * sizeof(float));
+        std::memcpy(&vw[to], v_weight + from, head_dim * sizeof(float));
+      }
+  return mapper_create(out, device, target_layers, target_heads, head_dim, num_selected, selected, kw.data(),
+                       k_bias, vw.data(), v_bias, source_heads);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Shared by the headwise and dense constructors: weights arrive per target
+// head as [L_t][H][KB * D][D] (KB = S headwise, S * src_heads dense).
+int mapper_create(cb_mapper** out, int device, int target_layers, int heads, int head_dim, int num_selected,
+                  const int64_t* selected, const float* k_weight, const float* k_bias, const float* v_weight,
+                  const float* v_bias, int src_heads) {
   if (out == nullptr) return fail(CB_ERR_INVALID, "null output handle");
   *out = nullptr;
   if (target_layers <= 0 || target_layers > CB_MAX_LAYERS)
@@ -414,6 +469,8 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
   m->H = heads;
   m->D = head_dim;
   m->S = num_selected;
+  m->Hs = src_heads;
+  m->KB = num_selected * (src_heads > 0 ? src_heads : 1);
   std::vector<int> sel(static_cast<size_t>(target_layers) * num_selected);
   for (size_t i = 0; i < sel.size(); ++i) {
     if (selected[i] < 0 || selected[i] >= CB_MAX_LAYERS) {
@@ -431,7 +488,7 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
   for (size_t i = 0; i < sel.size(); ++i)
     sel_local[i] = static_cast<int>(std::lower_bound(m->used.begin(), m->used.end(), sel[i]) - m->used.begin());
 
-  const int F = num_selected * head_dim;
+  const int F = m->KB * head_dim;
   const size_t w_per_kind = static_cast<size_t>(target_layers) * heads * F * head_dim;
   const size_t b_per_kind = static_cast<size_t>(target_layers) * heads * head_dim;
 
@@ -446,13 +503,15 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
     cb_mapper_destroy(m);
     return cuda_fail(err, what);
   };
-  if ((e = cudaMalloc(&m->w32, 2 * w_per_kind * sizeof(float))) != cudaSuccess) return cleanup(e, "cudaMalloc w32");
+  // FP32 weights feed the CUDA-core kernel, which is headwise only.
+  const bool keep_f32 = src_heads == 0;
+  if (keep_f32 && (e = cudaMalloc(&m->w32, 2 * w_per_kind * sizeof(float))) != cudaSuccess) return cleanup(e, "cudaMalloc w32");
   if ((e = cudaMalloc(&m->b32, 2 * b_per_kind * sizeof(float))) != cudaSuccess) return cleanup(e, "cudaMalloc b32");
   if ((e = cudaMalloc(&m->sel, sel.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc sel");
   if ((e = cudaMalloc(&m->sel_local, sel.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc sel_local");
   if ((e = cudaMalloc(&m->used_dev, m->used.size() * sizeof(int))) != cudaSuccess) return cleanup(e, "cudaMalloc used");
-  if ((e = cudaMemcpy(m->w32, k_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload k_weight");
-  if ((e = cudaMemcpy(m->w32 + w_per_kind, v_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload v_weight");
+  if (keep_f32 && (e = cudaMemcpy(m->w32, k_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload k_weight");
+  if (keep_f32 && (e = cudaMemcpy(m->w32 + w_per_kind, v_weight, w_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload v_weight");
   if ((e = cudaMemcpy(m->b32, k_bias, b_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload k_bias");
   if ((e = cudaMemcpy(m->b32 + b_per_kind, v_bias, b_per_kind * sizeof(float), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload v_bias");
   if ((e = cudaMemcpy(m->sel, sel.data(), sel.size() * sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload sel");
@@ -467,7 +526,7 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
     // K=16 step in no-swizzle K-major layout whose columns 0 and 1 hold
     // bf16(bias) and bf16(bias - bf16(bias)), so ones @ block == bias to ~2^-17.
     const size_t units = 2ull * target_layers * heads;
-    const size_t unit_halfs = (static_cast<size_t>(num_selected) * cbk::kKBlockBytes + cbk::kBiasBlockBytes) / 2;
+    const size_t unit_halfs = (static_cast<size_t>(m->KB) * cbk::kKBlockBytes + cbk::kBiasBlockBytes) / 2;
     std::vector<uint16_t> img(units * unit_halfs, 0);
     for (int kind = 0; kind < 2; ++kind) {
       const float* W = kind ? v_weight : k_weight;
@@ -478,7 +537,7 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
           const float* bh = B + (static_cast<size_t>(l) * heads + h) * head_dim;
           const size_t unit = (static_cast<size_t>(kind) * target_layers + l) * heads + h;
           uint16_t* base = img.data() + unit * unit_halfs;
-          for (int j = 0; j < num_selected; ++j) {
+          for (int j = 0; j < m->KB; ++j) {
             uint16_t* blk = base + static_cast<size_t>(j) * (cbk::kKBlockBytes / 2);
             for (int f = 0; f < 128; ++f) {
               const int panel = f >> 6, chunk = (f & 63) >> 3, e8 = f & 7;
@@ -490,7 +549,7 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
               }
             }
           }
-          uint16_t* bias_blk = base + static_cast<size_t>(num_selected) * (cbk::kKBlockBytes / 2);
+          uint16_t* bias_blk = base + static_cast<size_t>(m->KB) * (cbk::kKBlockBytes / 2);
           for (int d = 0; d < 128; ++d) {
             const uint16_t hi = f32_to_bf16_rne(bh[d]);
             uint32_t hbits = static_cast<uint32_t>(hi) << 16;
@@ -509,6 +568,10 @@ int cb_mapper_create(cb_mapper** out, int device, int target_layers, int heads, 
   *out = m;
   return CB_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int cb_mapper_destroy(cb_mapper* m) {
   if (m == nullptr) return CB_OK;
@@ -561,7 +624,9 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
   if (n_tokens > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "too many tokens in one call");
   const bool tc = (m->D == cbk::kD && dtype == CB_DTYPE_BF16);
   int rc;
-  if ((rc = check_rows(src, "src", m->D, m->H, dtype, tc)) != CB_OK) return rc;
+  if (m->Hs > 0 && !tc)
+    return fail(CB_ERR_UNSUPPORTED, "dense (nv_transfer) mappers run on the tensor-core path only (bf16, head_dim 128)");
+  if ((rc = check_rows(src, "src", m->D, ws_heads(m), dtype, tc)) != CB_OK) return rc;
   if ((rc = check_rows(dst, "dst", m->D, m->H, dtype, tc)) != CB_OK) return rc;
   if (src->layers <= m->max_sel) return fail(CB_ERR_INVALID, "mapper selected layer exceeds source page depth");
   if (dst->layers != m->L_t) return fail(CB_ERR_INVALID, "destination layer count != mapper target layers");

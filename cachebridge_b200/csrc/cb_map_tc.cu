@@ -178,7 +178,11 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
         flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
         valid = 0;
       }
-      for (int j = 0; j < p.S; ++j) {
+      for (int kb = 0; kb < p.KB; ++kb) {
+        // Feature block kb: selected layer j, source head sh (the target head
+        // itself for headwise maps, every source head in turn for dense ones).
+        const int j = kb / p.kb_heads;
+        const int sh = p.dense ? kb - j * p.kb_heads : it.h;
         // Warp-uniform outcome: the gather below uses full-warp shuffles.
         const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), phase ^ 1u, s.abort_flag, p.status);
         if (!__all_sync(0xffffffffu, got)) {
@@ -191,14 +195,14 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
           if (leader) {
             const int u = __ldg(p.sel_local + it.l * p.S + j);
             mbar_arrive_expect_tx(full, kKBlockBytes);
-            tma_load_4d(dst, &p.kmap, 0, it.h, tok0, u, full);
-            tma_load_4d(dst + kPanelBytes, &p.kmap, 64, it.h, tok0, u, full);
+            tma_load_4d(dst, &p.kmap, 0, sh, tok0, u, full);
+            tma_load_4d(dst + kPanelBytes, &p.kmap, 64, sh, tok0, u, full);
           }
           mbar_arrive(full);
         } else {
           const int sl = __ldg(p.sel_global + it.l * p.S + j);
           const char* base = reinterpret_cast<const char*>(p.src_v[sl]) +
-                             static_cast<int64_t>(p.src_head_offset + it.h) * (kD * 2);
+                             static_cast<int64_t>(p.src_head_offset + sh) * (kD * 2);
           const int64_t stride_bytes = p.src_row_stride * 2;
           const int c = lane & 15;
 #pragma unroll
@@ -238,11 +242,11 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
     const uint8_t* wu = p.w_img + static_cast<int64_t>((it.kind * p.L_t + it.l) * p.H + it.h) * p.unit_bytes;
     if (!mbar_wait(bar_at(s, kBarBEmpty), (itc & 1) ^ 1, s.abort_flag, p.status)) break;
     mbar_arrive_expect_tx(bar_at(s, kBarBFull), kBiasBlockBytes);
-    bulk_copy_g2s(s.bias, wu + static_cast<int64_t>(p.S) * kKBlockBytes, kBiasBlockBytes, bar_at(s, kBarBFull),
+    bulk_copy_g2s(s.bias, wu + static_cast<int64_t>(p.KB) * kKBlockBytes, kBiasBlockBytes, bar_at(s, kBarBFull),
                   policy);
     last_par[4] = itc & 1;
     if (p.w_resident) {
-      for (int j = 0; j < p.S; ++j) {
+      for (int j = 0; j < p.KB; ++j) {
         if (!mbar_wait(bar_at(s, kBarWEmpty + j), (itc & 1) ^ 1, s.abort_flag, p.status)) {
           ok = false;
           break;
@@ -254,7 +258,7 @@ __device__ void run_weight_loader(const MapTcParams& p, const Smem& s) {
       }
     } else {
       for (int m = 0; m < it.mtiles && ok; ++m) {
-        for (int j = 0; j < p.S; ++j) {
+        for (int j = 0; j < p.KB; ++j) {
           const int slot = wq & 1;
           if (!mbar_wait(bar_at(s, kBarWEmpty + slot), ((wq >> 1) & 1) ^ 1, s.abort_flag, p.status)) {
             ok = false;
@@ -312,7 +316,7 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
       const uint32_t d_tmem = tmem_base + acc * kD;
       // Accumulator := ones[:, 0:2] @ [bias_hi; bias_lo] = bias (FP32).
       umma_bf16(d_tmem, ones_desc, bias_desc, idesc, 0u);
-      for (int j = 0; j < p.S; ++j) {
+      for (int j = 0; j < p.KB; ++j) {
         int wslot;
         if (p.w_resident) {
           wslot = j;
@@ -358,7 +362,7 @@ __device__ void run_mma(const MapTcParams& p, const Smem& s, uint32_t tmem_base)
     if (ok) {
       umma_commit(bar_at(s, kBarBEmpty));
       if (p.w_resident)
-        for (int j = 0; j < p.S; ++j) umma_commit(bar_at(s, kBarWEmpty + j));
+        for (int j = 0; j < p.KB; ++j) umma_commit(bar_at(s, kBarWEmpty + j));
     }
     ++itc;
   }

@@ -29,6 +29,10 @@ struct MapTcParams {
   int L_t;       // target layers
   int H;         // heads mapped by this call
   int S;         // selected source layers per target layer
+  int KB;        // 128-feature blocks per unit: S (headwise) or S * source heads (dense)
+  int kb_heads;  // source heads per selected layer in the block sequence (1 headwise)
+  int dense;     // 1: block kb reads source head kb % kb_heads; 0: the target head
+  int ws_heads;  // heads per row of the key workspace and of the source rows read
   int R;         // m-tiles per chunk
   int n_chunks;
   int num_items;
@@ -36,8 +40,8 @@ struct MapTcParams {
   int stages;    // A stages (ring)
   int w_resident;
 
-  const uint8_t* w_img;     // per unit: S x 32 KB W^T k-blocks (128B-swizzled) + 4 KB bias block
-  int64_t unit_bytes;       // S * 32 KB + 4 KB
+  const uint8_t* w_img;     // per unit: KB x 32 KB W^T k-blocks (128B-swizzled) + 4 KB bias block
+  int64_t unit_bytes;       // KB * 32 KB + 4 KB
   const int* sel_global;    // [L_t][S] source layer ids
   const int* sel_local;     // [L_t][S] index into the workspace's used-layer list
 

@@ -63,6 +63,47 @@ def _pad_selected(layers: list[LayerWeights], head_dim: int):
     return S, selected, kw, kb, vw, vb
 
 
+def _dense_source_heads(layers: list[LayerWeights], heads: int, head_dim: int) -> int:
+    """Source heads per selected layer of dense (nv_transfer) layers, whose
+    k_weight is [S * source_heads * D, heads, D] (mapper.py:182-203)."""
+    found = None
+    for layer in layers:
+        s = int(layer.selected.numel())
+        f = int(layer.k_weight.shape[0])
+        if (layer.k_weight.ndim != 3 or tuple(layer.k_weight.shape[1:]) != (heads, head_dim)
+                or tuple(layer.v_weight.shape) != tuple(layer.k_weight.shape) or f % (s * head_dim)):
+            raise ValueError("NV Dense feature-width mismatch")
+        hs = f // (s * head_dim)
+        if found is not None and hs != found:
+            raise ValueError("NV Dense feature-width mismatch")
+        found = hs
+    return found
+
+
+def _pad_dense(layers: list[LayerWeights], source_heads: int, head_dim: int):
+    """Uniform [L_t][S] selections and [L_t][S*Hs*D][H][D] weights; layers with
+    fewer selected source layers repeat their first one with zero weights."""
+    S = max(int(layer.selected.numel()) for layer in layers)
+    L_t = len(layers)
+    H = int(layers[0].k_bias.shape[0])
+    block = source_heads * head_dim
+    selected = np.zeros((L_t, S), dtype=np.int64)
+    kw = np.zeros((L_t, S * block, H, head_dim), dtype=np.float32)
+    vw = np.zeros_like(kw)
+    kb = np.zeros((L_t, H, head_dim), dtype=np.float32)
+    vb = np.zeros_like(kb)
+    for i, layer in enumerate(layers):
+        sel = layer.selected.tolist()
+        s = len(sel)
+        selected[i, :s] = sel
+        selected[i, s:] = sel[0]
+        kw[i, : s * block] = layer.k_weight.float().cpu().numpy()
+        vw[i, : s * block] = layer.v_weight.float().cpu().numpy()
+        kb[i] = layer.k_bias.float().cpu().numpy()
+        vb[i] = layer.v_bias.float().cpu().numpy()
+    return S, selected, kw, kb, vw, vb
+
+
 class PageMapper:
     """Apply CacheBridge mapper files to SGLang pages on a B200.
 
@@ -142,44 +183,47 @@ class PageMapper:
                     headwise=headwise,
                 )
             )
-        if method != "cachebridge":
-            raise NotImplementedError(
-                "only the CacheBridge (headwise) mapper runs on the B200 handoff path; "
-                "the dense nv_transfer mode is not implemented"
-            )
+        self.dense = method != "cachebridge"
         if self.device.type != "cuda":
             raise ValueError("cachebridge_b200 runs on CUDA devices only")
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.head_dim = int(self.layers[0].k_bias.shape[1])
         self.heads = self.target_head_stop - self.target_head_start
+        self.source_heads = self.heads  # source heads read per selected layer
         for layer in self.layers:
             sel = layer.selected
             if sel.ndim != 1 or sel.numel() == 0 or int(sel.min()) < 0:
                 raise ValueError("mapper selected layer list must be non-empty and non-negative")
-            if tuple(layer.k_weight.shape) != (self.heads, sel.numel() * self.head_dim, self.head_dim):
+            if not self.dense and tuple(layer.k_weight.shape) != (self.heads, sel.numel() * self.head_dim,
+                                                                  self.head_dim):
                 raise ValueError("CacheBridge source-head geometry mismatch")
+        if self.dense:
+            self.source_heads = _dense_source_heads(self.layers, self.heads, self.head_dim)
         self.max_selected = max(int(layer.selected.max()) for layer in self.layers)
-        S, selected, kw, kb, vw, vb = _pad_selected(self.layers, self.head_dim)
-        self.num_selected = S
         lib = nat.load()
         handle = ctypes.c_void_p()
-        nat.check(
-            lib.cb_mapper_create(
-                ctypes.byref(handle),
-                self.device.index,
-                len(self.layers),
-                self.heads,
-                self.head_dim,
-                S,
-                selected.ctypes.data,
-                kw.ctypes.data,
-                kb.ctypes.data,
-                vw.ctypes.data,
-                vb.ctypes.data,
-            ),
-            "cb_mapper_create",
-        )
+        if self.dense:
+            S, selected, kw, kb, vw, vb = _pad_dense(self.layers, self.source_heads, self.head_dim)
+            self.num_selected = S
+            nat.check(
+                lib.cb_mapper_create_dense(
+                    ctypes.byref(handle), self.device.index, len(self.layers), self.heads, self.source_heads,
+                    self.head_dim, S, selected.ctypes.data, kw.ctypes.data, kb.ctypes.data, vw.ctypes.data,
+                    vb.ctypes.data,
+                ),
+                "cb_mapper_create_dense",
+            )
+        else:
+            S, selected, kw, kb, vw, vb = _pad_selected(self.layers, self.head_dim)
+            self.num_selected = S
+            nat.check(
+                lib.cb_mapper_create(
+                    ctypes.byref(handle), self.device.index, len(self.layers), self.heads, self.head_dim, S,
+                    selected.ctypes.data, kw.ctypes.data, kb.ctypes.data, vw.ctypes.data, vb.ctypes.data,
+                ),
+                "cb_mapper_create",
+            )
         self._handle = handle
 
     @classmethod
@@ -266,16 +310,23 @@ class PageMapper:
         """Map one page; same contract as the reference's ``map_page``.
 
         ``source_page`` is ``[2, source_layers, tokens, source_heads, head_dim]``
-        (keys RoPE-applied); the received shard is narrowed to this rank's
-        heads first (online/mapping.py:18-28). Returns (or fills ``output``
+        (keys RoPE-applied). A headwise mapper narrows the received shard to
+        this rank's heads first (online/mapping.py:18-28); a dense one reads
+        every source head. Returns (or fills ``output``
         with) ``[2, target_layers, tokens, heads, head_dim]`` in the page dtype.
         """
         if source_page.ndim != 5 or source_page.shape[0] != 2:
             raise ValueError("source page must be [2,layers,tokens,kv_heads,head_dim]")
-        start = self.target_head_start - source_head_offset
-        stop = self.target_head_stop - source_head_offset
-        if not 0 <= start < stop <= source_page.shape[3]:
-            raise ValueError("Received source shard does not contain required heads")
+        if self.dense:
+            # Dense maps read every source head of the page (mapper.py:182-203).
+            if source_page.shape[3] != self.source_heads:
+                raise ValueError("NV Dense feature-width mismatch")
+            start = 0
+        else:
+            start = self.target_head_start - source_head_offset
+            stop = self.target_head_stop - source_head_offset
+            if not 0 <= start < stop <= source_page.shape[3]:
+                raise ValueError("Received source shard does not contain required heads")
         dtype = source_page.dtype
         storage_dtype_code(dtype)
         _, source_layers, tokens, _, head_dim = source_page.shape

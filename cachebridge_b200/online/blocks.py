@@ -134,9 +134,10 @@ def map_install_block(
         raise ValueError("invalid block span")
     if target_pool.layer_num != mapper.target_layers or target_pool.dtype != source_pool.dtype:
         raise ValueError("mapper output geometry/dtype mismatch")
-    head_start = mapper.target_head_start - source_head_offset
+    # Headwise maps read this rank's heads of the source rows; dense maps all of them.
+    head_start = 0 if mapper.dense else mapper.target_head_start - source_head_offset
     src = RowSet.from_pool(source_pool, source_indices[start:stop], head_offset=head_start)
-    if not 0 <= head_start < head_start + mapper.heads <= src.heads:
+    if not 0 <= head_start < head_start + mapper.source_heads <= src.heads:
         raise ValueError("Received source shard does not contain required heads")
     if hasattr(target_pool, "rows"):  # TokenKVPool, or a peer pool mapped through CUDA IPC
         dst = target_pool.rows(target_indices[start:stop], target_head_offset)

@@ -123,6 +123,23 @@ CB_API int cb_mapper_create(cb_mapper** out, int device, int target_layers, int 
                      int head_dim, int num_selected, const int64_t* selected,
                      const float* k_weight, const float* k_bias,
                      const float* v_weight, const float* v_bias);
+/*
+ * Upload one dense ("nv_transfer") mapper for a target TP rank. Replaces
+ * PageMapper.__init__ for non-headwise layer files (src/cachebridge/mapper.py:59-110
+ * with the dense branch of map_page, mapper.py:182-203): every target head
+ * reads all source_heads heads of each selected source layer.
+ *   selected [target_layers][num_selected] int64
+ *   k_weight, v_weight [target_layers][num_selected*source_heads*head_dim][target_heads][head_dim]
+ *     (the reference's k_weight[:, head_slice])
+ *   k_bias, v_bias [target_layers][target_heads][head_dim]
+ * head_dim must be 128 and num_selected*source_heads at most 64; the map runs
+ * on the tensor-core path only (BF16 storage). cb_map_install then reads
+ * source heads src->head_offset .. +source_heads of every source row.
+ */
+CB_API int cb_mapper_create_dense(cb_mapper** out, int device, int target_layers, int target_heads,
+                                  int source_heads, int head_dim, int num_selected,
+                                  const int64_t* selected, const float* k_weight, const float* k_bias,
+                                  const float* v_weight, const float* v_bias);
 /* Free a mapper and its device memory. */
 CB_API int cb_mapper_destroy(cb_mapper* mapper);
 /* Geometry of an uploaded mapper (any output pointer may be NULL). */

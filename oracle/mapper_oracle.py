@@ -5,7 +5,8 @@ PyTorch on the CPU, the reference's algorithm for the online handoff path:
 
   qwen_rope                 src/cachebridge/rope.py:16-72
   rotate_half/apply/remove  src/cachebridge/rope.py:9-13, 75-89
-  PageMapper.map_page       src/cachebridge/mapper.py:116-181 (headwise branch)
+  PageMapper.map_page       src/cachebridge/mapper.py:116-181 (headwise branch),
+                            182-203 (dense nv_transfer branch)
                             and 207-239 (stack, target RoPE, cast to page dtype),
                             after the head narrowing of online/mapping.py:7-33
   pack_source_block         src/cachebridge/online/blocks.py:47-82
@@ -106,13 +107,16 @@ def load_layers(mapper_dir, *, tp_rank: int = 0, tp_size: int = 1):
         rng = (tp_rank * per, tp_rank * per + per)
         head_range = head_range or rng
         sl = slice(*rng)
+        headwise = "headwise" in t
         layers.append(
             dict(
                 selected=t["selected"].long().tolist(),
-                k_weight=t["k_weight"][sl].float(),
+                # headwise [H, S*D, D] sliced by head; dense [F, H, D] by column (mapper.py:97-107)
+                k_weight=(t["k_weight"][sl] if headwise else t["k_weight"][:, sl]).float(),
                 k_bias=t["k_bias"][sl].float(),
-                v_weight=t["v_weight"][sl].float(),
+                v_weight=(t["v_weight"][sl] if headwise else t["v_weight"][:, sl]).float(),
                 v_bias=t["v_bias"][sl].float(),
+                headwise=headwise,
             )
         )
     return layers, head_range
@@ -134,12 +138,17 @@ def map_page_f32(
     source_scaling: dict | None = None,
     target_scaling: dict | None = None,
 ) -> torch.Tensor:
-    """FP32 mapped page ``[2, L_t, n, H_r, D]`` before the storage-dtype cast."""
-    start = head_range[0] - source_head_offset
-    stop = head_range[1] - source_head_offset
-    if not 0 <= start < stop <= page.shape[3]:
-        raise ValueError("Received source shard does not contain required heads")
-    page = page[:, :, :, start:stop, :]
+    """FP32 mapped page ``[2, L_t, n, H_r, D]`` before the storage-dtype cast.
+
+    Headwise layers read this rank's heads of the page (online/mapping.py:18-28);
+    dense (nv_transfer) layers read every source head (mapper.py:182-203)."""
+    dense = bool(layers) and not layers[0].get("headwise", True)
+    if not dense:
+        start = head_range[0] - source_head_offset
+        stop = head_range[1] - source_head_offset
+        if not 0 <= start < stop <= page.shape[3]:
+            raise ValueError("Received source shard does not contain required heads")
+        page = page[:, :, :, start:stop, :]
     _, L_s, n, _, D = page.shape
     positions = torch.arange(position_start, position_start + n, dtype=torch.long)
     scos, ssin = qwen_rope(positions, head_dim=D, theta=source_theta, scaling=source_scaling)
@@ -150,10 +159,19 @@ def map_page_f32(
         sel = layer["selected"]
         if not sel or max(sel) >= L_s:
             raise ValueError("mapper selected layer exceeds source page depth")
-        xk = torch.cat([keys[i] for i in sel], dim=-1)
-        xv = torch.cat([values[i] for i in sel], dim=-1)
-        out_k.append(torch.einsum("thf,hfd->thd", xk, layer["k_weight"]) + layer["k_bias"])
-        out_v.append(torch.einsum("thf,hfd->thd", xv, layer["v_weight"]) + layer["v_bias"])
+        if layer.get("headwise", True):
+            xk = torch.cat([keys[i] for i in sel], dim=-1)
+            xv = torch.cat([values[i] for i in sel], dim=-1)
+            out_k.append(torch.einsum("thf,hfd->thd", xk, layer["k_weight"]) + layer["k_bias"])
+            out_v.append(torch.einsum("thf,hfd->thd", xv, layer["v_weight"]) + layer["v_bias"])
+        else:
+            xk = torch.cat([keys[i].reshape(n, -1) for i in sel], dim=-1)
+            xv = torch.cat([values[i].reshape(n, -1) for i in sel], dim=-1)
+            if xk.shape[-1] != layer["k_weight"].shape[0]:
+                raise ValueError("NV Dense feature-width mismatch")
+            h, d = layer["k_bias"].shape
+            out_k.append((xk @ layer["k_weight"].reshape(xk.shape[-1], -1) + layer["k_bias"].reshape(-1)).reshape(n, h, d))
+            out_v.append((xv @ layer["v_weight"].reshape(xv.shape[-1], -1) + layer["v_bias"].reshape(-1)).reshape(n, h, d))
     tk = torch.stack(out_k, dim=0)
     tv = torch.stack(out_v, dim=0)
     tcos, tsin = qwen_rope(positions, head_dim=tk.shape[-1], theta=target_theta, scaling=target_scaling)

@@ -29,6 +29,9 @@ MAPPER_CASES = [
     "qwen_s8_compact",
 ]
 
+# Dense (nv_transfer) mapper fixtures, produced by the reference's dense branch.
+DENSE_CASES = ["dense_mini_bf16", "dense_small_f32"]
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")

@@ -3,7 +3,7 @@
 Run in the build container, where the reference source tree is importable:
 
     PYTHONDONTWRITEBYTECODE=1 PYTHONPATH=<reference>/src \
-        python tests/golden/make_golden.py <reference>
+        python tests/golden/make_golden.py <reference> [dense]
 
 Each case directory under tests/golden/ holds the mapper files in the
 reference's ``layer_NNN.safetensors`` format, ``case.safetensors`` (inputs and
@@ -146,6 +146,46 @@ def random_case(ref, name, *, seed, L_s, L_t, H, D, S, n, dtype, position_start,
     return out
 
 
+def dense_case(ref, name, *, seed, L_s, L_t, Hs, H, D, S, n, dtype, position_start, theta, tp_rank=0,
+               tp_size=1, bf16_weights=False):
+    """Dense (nv_transfer) layers: k_weight [S*Hs*D, H, D] without a headwise
+    key, mapped by the reference's PageMapper(method="nv_transfer")."""
+    g = torch.Generator().manual_seed(seed)
+    d = _case_dir(name)
+    F = S * Hs * D
+    layers = []
+    for _ in range(L_t):
+        sel = torch.randperm(L_s, generator=g)[:S]
+        t = dict(selected=sel.long())
+        for kind in ("k", "v"):
+            w = torch.randn(F, H, D, generator=g) / F**0.5
+            b = torch.randn(H, D, generator=g) * 0.1
+            if bf16_weights:
+                w, b = w.bfloat16(), b.bfloat16()
+            t[f"{kind}_weight"], t[f"{kind}_bias"] = w, b
+        layers.append(t)
+    _write_layers(d, layers)
+    page = _source_page(ref, g, L_s=L_s, n=n, H=Hs, D=D, theta=theta, scaling=None,
+                        position_start=position_start, dtype=dtype, lognormal=True)
+    mapper = ref.PageMapper(d, method="nv_transfer", source_rope_theta=theta, target_rope_theta=theta,
+                            target_tp_rank=tp_rank, target_tp_size=tp_size)
+    out = mapper.map_page(page, position_start=position_start)
+    params = dict(position_start=position_start, source_theta=theta, target_theta=theta, source_scaling=None,
+                  target_scaling=None, tp_rank=tp_rank, tp_size=tp_size, source_head_offset=0,
+                  method="nv_transfer")
+    _save(d, params, dict(page=page, expected=out))
+    return out
+
+
+def dense_cases(ref):
+    # Dense maps read every source head: 4 source heads, 4 target heads, TP rank 1 of 2.
+    dense_case(ref, "dense_mini_bf16", seed=31, L_s=5, L_t=2, Hs=4, H=4, D=128, S=2, n=96,
+               dtype=torch.bfloat16, position_start=700, theta=1e6, tp_rank=1, tp_size=2, bf16_weights=True)
+    # FP32 storage, different source and target head counts (oracle pin; the B200 dense path is BF16 only).
+    dense_case(ref, "dense_small_f32", seed=32, L_s=3, L_t=2, Hs=3, H=2, D=64, S=1, n=20,
+               dtype=torch.float32, position_start=3, theta=1e4)
+
+
 def reference_unit_cases(ref):
     """Re-creations of tests/test_mapper.py:66-105 (headwise identity, TP slice, YaRN)."""
     # tests/test_mapper.py:38-50 headwise identity mapper, 10-18 rotated page (seed 7).
@@ -266,6 +306,10 @@ def main(argv):
         raise SystemExit(__doc__)
     ref = _reference(argv[1])
     torch.set_num_threads(4)
+    if len(argv) > 2 and argv[2] == "dense":  # only the dense (nv_transfer) cases
+        dense_cases(ref)
+        print("dense golden fixtures written to", HERE)
+        return
     reference_unit_cases(ref)
     fit_cases(ref)
     pack_case(ref)
@@ -295,6 +339,7 @@ def main(argv):
                 dtype=torch.bfloat16, position_start=7, source_theta=1e6, target_theta=1e6, tp_rank=1,
                 tp_size=2, source_head_offset=1, page_heads=1, w_var=1 / 1024, lognormal=True,
                 bf16_weights=True)
+    dense_cases(ref)
     print("golden fixtures written to", HERE)
 
 

@@ -11,11 +11,11 @@ import json
 import pytest
 import torch
 
-from conftest import GOLDEN, MAPPER_CASES, load_case, oracle_kwargs
+from conftest import DENSE_CASES, GOLDEN, MAPPER_CASES, load_case, oracle_kwargs
 from oracle import mapper_oracle as orc
 
 
-@pytest.mark.parametrize("name", MAPPER_CASES)
+@pytest.mark.parametrize("name", MAPPER_CASES + DENSE_CASES)
 def test_oracle_matches_reference_map_page(name):
     d, params, t = load_case(name)
     layers, head_range = orc.load_layers(d, tp_rank=params.get("tp_rank", 0), tp_size=params.get("tp_size", 1))
