@@ -513,7 +513,8 @@ def run_sharded(args):
     peer_pool = placement = handoff = None
     if target_side:
         placement = tp.TargetPlacement(plan, requests, chunk=chunk, source_layers=L_s, device=dev, group=host_group,
-                                       source_pool=src_pool, mapper=mapper, target_pool=dst_pool)
+                                       source_pool=src_pool, mapper=mapper, target_pool=dst_pool,
+                                       transport=args.transport)
         runner = placement
     else:
         peer_pool = tp.exchange_target_pools(plan, dst_pool, group=host_group, device=dev)
@@ -616,8 +617,10 @@ def run_sharded(args):
     achieved = shard_bytes / (statistics.mean(step_ms) / 1e3) / 1e9
     if rank == 0:
         h2d = sum(s.numel() * s.element_size() + t.numel() * t.element_size() for s, t in host_idx)
-        transport = ("source rows packed into the target GPU's receive slots (peer stores, CUDA IPC), mapped and "
-                     "installed on the target" if target_side else
+        transport = (("source rows gathered locally, moved by one copy-engine transfer per chunk into the target "
+                      "GPU's receive slots (CUDA IPC), mapped and installed on the target" if args.transport == "copy_engine"
+                      else "source rows packed into the target GPU's receive slots (peer stores, CUDA IPC), mapped "
+                      "and installed on the target") if target_side else
                      "map kernel stores into the peer target pool (CUDA IPC, NVLink)")
         line = dict(
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
@@ -625,6 +628,7 @@ def run_sharded(args):
             dtype="bf16", data="synthetic",
             config=dict(workload=f"qwen3-14b->32b sharded handoff (BASELINE config 3), TP{plan.tp}+TP{plan.tp}",
                         requests=n_req, request_tokens=n_tok, chunk_tokens=chunk, source_layers=L_s,
+                        transport_mode=args.transport if target_side else "peer_stores",
                         target_layers=L_t, kv_heads=H, heads_per_rank=Hr, head_dim=D, selected=S,
                         pool_slots=rows, page_size=1, slot_lists="seeded random", placement=args.placement,
                         transport=transport, l2="inputs larger than L2",
@@ -632,8 +636,8 @@ def run_sharded(args):
             latency_p50_ms=statistics.median(step_ms),
             roofline=dict(bound="nvlink", achieved=achieved, peak=nvlink_peak, unit="GB/s",
                           frac=achieved / nvlink_peak, traffic=None,
-                          kernel=("copy_rows_kernel peer stores" if target_side
-                                  else "map_install_tc_kernel peer stores") + " (one pair, per direction)",
+                          kernel=(("copy-engine transfers" if args.transport == "copy_engine" else "copy_rows_kernel peer stores")
+                                  if target_side else "map_install_tc_kernel peer stores") + " (one pair, per direction)",
                           shard_bytes_per_pair=shard_bytes, peak_source="recipe-measured peer copy"),
             cpu_baseline=None,
             e2e=dict(value=total / (float(e2e_ms) / 1e3), unit=UNIT, h2d_bytes_per_step=h2d,
@@ -671,6 +675,8 @@ def main(argv=None):
     ap.add_argument("--request-tokens", type=int, default=32768, help="history tokens per request (N>1)")
     ap.add_argument("--chunk", type=int, default=2048, help="tokens per map+install call (N>1)")
     ap.add_argument("--pool-slack", type=int, default=4096, help="free pool rows beyond the requests (N>1)")
+    ap.add_argument("--transport", choices=["copy_engine", "peer_stores"], default="peer_stores",
+                    help="N>1 target placement: staged chunks moved by the copy engine, or gather-kernel peer stores")
     ap.add_argument("--placement", choices=["target", "source"], default="target",
                     help="N>1: map on the target GPU (raw source rows cross NVLink) or on the source GPU")
     args = ap.parse_args(argv)

@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "cb_ipc_export",
     "cb_ipc_open",
     "cb_ipc_close",
+    "cb_copy_async",
     "cb_chunk_signal",
     "cb_chunk_wait",
     "cb_enable_peer_access",
@@ -144,6 +145,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_ipc_export.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]
     lib.cb_ipc_open.restype = c_int
     lib.cb_ipc_open.argtypes = [c_vp, c_int, ctypes.POINTER(c_vp)]
+    lib.cb_copy_async.restype = c_int
+    lib.cb_copy_async.argtypes = [c_vp, c_vp, c_vp, c_size]
     lib.cb_chunk_signal.restype = c_int
     lib.cb_chunk_signal.argtypes = [c_vp, c_vp, c_i64]
     lib.cb_chunk_wait.restype = c_int

@@ -874,6 +874,19 @@ int cb_ipc_close(void* ptr) {
   return CB_OK;
 }
 
+int cb_copy_async(void* stream, void* dst, const void* src, size_t bytes) {
+  if (bytes == 0) return CB_OK;
+  if (dst == nullptr || src == nullptr) return fail(CB_ERR_INVALID, "null copy pointer");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(CB_ERR_CUDA, "cudaGetDevice failed");
+  int rc = ensure_access(device, dst, "copy destination");
+  if (rc != CB_OK) return rc;
+  if ((rc = ensure_access(device, src, "copy source")) != CB_OK) return rc;
+  const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync");
+  return CB_OK;
+}
+
 int cb_chunk_signal(void* stream, int64_t* flag, int64_t value) {
   if (flag == nullptr) return fail(CB_ERR_INVALID, "null flag");
   if (reinterpret_cast<uintptr_t>(flag) % 8) return fail(CB_ERR_INVALID, "flag not 8-byte aligned");

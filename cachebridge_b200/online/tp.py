@@ -254,9 +254,11 @@ class TargetPlacement:
     """Target-side placement for one source/target pair.
 
     The source rank gathers each chunk's raw source KV rows (its H_r heads of
-    every source layer) and stores them contiguously into one of two receive
-    slots on the target GPU (``cb_pack_rows`` with a peer output: coalesced
-    NVLink stores); the target rank maps the received block into its own pool
+    every source layer) into one of two receive slots on the target GPU:
+    either stored straight into the peer slot by the gather kernel
+    (``transport="peer_stores"``, the default: coalesced NVLink stores,
+    691 GB/s at TP1+TP1), or staged locally and moved by one copy-engine
+    transfer per chunk on a second stream (``"copy_engine"``: 603 GB/s). The target rank maps the received block into its own pool
     (``cb_map_install``: derotation, map, target RoPE, install through the
     slot table). Raw source rows are 2*L_s*H_r*D*2 bytes per token against
     2*L_t*H_r*D*2 mapped, so fewer bytes cross NVLink than with source-side
@@ -278,11 +280,15 @@ class TargetPlacement:
     SLOTS = 2
 
     def __init__(self, plan: PairPlan, requests, *, chunk: int, source_layers: int, device: torch.device,
-                 group=None, source_pool=None, mapper=None, target_pool=None, timeout_s: float = 10.0):
+                 group=None, source_pool=None, mapper=None, target_pool=None, timeout_s: float = 10.0,
+                 transport: str = "peer_stores"):
         from .. import _native as nat
         from ..device import storage_dtype_code
 
+        if transport not in ("copy_engine", "peer_stores"):
+            raise ValueError("transport must be 'copy_engine' or 'peer_stores'")
         self.plan = plan
+        self.transport = transport
         self.device = torch.device(device)
         self.lib = nat.load()
         self.timeout_ns = int(timeout_s * 1e9)
@@ -330,6 +336,16 @@ class TargetPlacement:
                 rs = RowSet.from_pool(source_pool, requests[q][0][a:b])
                 self.src_rows.append((rs, rs.to_c()))
             self.row_heads = source_pool.heads
+            self.chunk_bytes = [2 * source_layers * (b - a) * H * D * elem for _, a, b in self.chunks]
+            if transport == "copy_engine":
+                # Packed chunks are staged locally, then one copy-engine transfer
+                # per chunk moves them over NVLink on a second stream while the
+                # next chunk is gathered.
+                self.staging = torch.empty((self.SLOTS, slot_elems), dtype=dtype, device=self.device)
+                self.copy_stream = torch.cuda.Stream(self.device)
+                self.packed = [torch.cuda.Event() for _ in range(self.SLOTS)]
+                self.copied = [torch.cuda.Event() for _ in range(self.SLOTS)]
+                self.copied_recorded = [False] * self.SLOTS
         else:
             consumed = _Mapped(peer["consumed"], self.device)
             self._mapped = [consumed]
@@ -363,7 +379,9 @@ class TargetPlacement:
         for i in range(len(self.chunks)):
             c = self.counter
             slot = i % self.SLOTS  # fixed per chunk: the target's prepared calls read it
-            if self.plan.role == "source":
+            if self.plan.role == "source" and self.transport == "copy_engine":
+                self._send_staged(i, slot, c, st, status)
+            elif self.plan.role == "source":
                 # The chunk that last used this slot must have been consumed.
                 nat.check(self.lib.cb_chunk_wait(st, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot),
                                                  self.last_use[slot], self.timeout_ns, status), "cb_chunk_wait")
@@ -381,6 +399,37 @@ class TargetPlacement:
                           "cb_chunk_signal")
             self.last_use[slot] = c
             self.counter += 1
+        if self.plan.role == "source" and self.transport == "copy_engine":
+            # Later work on the caller's stream (the vote) follows every transfer.
+            current = torch.cuda.current_stream(self.device)
+            for slot in range(self.SLOTS):
+                if self.copied_recorded[slot]:
+                    current.wait_event(self.copied[slot])
+
+    def _send_staged(self, i: int, slot: int, c: int, st, status: int) -> None:
+        """Gather chunk i into local staging slot `slot` on the caller's stream,
+        then (copy stream) wait until the target consumed the receive slot's
+        previous chunk, copy the chunk over NVLink and signal its arrival."""
+        from .. import _native as nat
+
+        current = torch.cuda.current_stream(self.device)
+        if self.copied_recorded[slot]:
+            current.wait_event(self.copied[slot])  # the staging slot's last transfer is done
+        rs, crow = self.src_rows[i]
+        staged = self.staging[slot].data_ptr()
+        nat.check(self.lib.cb_pack_rows(st, ctypes.byref(crow), self.head_dim, self.dtype_code, rs.slots.numel(),
+                                        ctypes.c_void_p(staged), status), "cb_pack_rows")
+        self.packed[slot].record(current)
+        cs = self.copy_stream
+        cs.wait_event(self.packed[slot])
+        cst = ctypes.c_void_p(cs.cuda_stream)
+        nat.check(self.lib.cb_chunk_wait(cst, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot), self.last_use[slot],
+                                         self.timeout_ns, status), "cb_chunk_wait")
+        nat.check(self.lib.cb_copy_async(cst, ctypes.c_void_p(self.peer_recv[slot]), ctypes.c_void_p(staged),
+                                         self.chunk_bytes[i]), "cb_copy_async")
+        nat.check(self.lib.cb_chunk_signal(cst, ctypes.c_void_p(self.peer_ready[slot]), c), "cb_chunk_signal")
+        self.copied[slot].record(cs)
+        self.copied_recorded[slot] = True
 
     def close(self) -> None:
         """Unmap the peer buffers (after this rank's stream work finished)."""

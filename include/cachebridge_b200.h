@@ -286,6 +286,14 @@ CB_API int cb_ipc_export(const void* device_ptr, void* handle_out /* 64 bytes */
 CB_API int cb_ipc_open(const void* handle /* 64 bytes */, int device, void** ptr_out);
 CB_API int cb_ipc_close(void* ptr);
 /*
+ * One asynchronous copy of `bytes` contiguous bytes on `stream` (the copy
+ * engines; either side may be a peer device's memory, with peer access
+ * enabled first). Replaces the ctypes cudaMemcpyPeerAsync of
+ * backends/sglang/runtime/peer_runtime.py:34-64 for whole packed chunks.
+ */
+CB_API int cb_copy_async(void* stream, void* dst, const void* src, size_t bytes);
+
+/*
  * Device-side chunk handshake between two GPUs (the double-buffered
  * source -> target pipeline). Both launch one thread on the caller's stream
  * on the current device; `flag` is an 8-byte aligned int64 counter in device

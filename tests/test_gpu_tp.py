@@ -2,7 +2,9 @@
   - source placement: rank 0 maps into rank 1's pool through CUDA IPC peer
     stores (NVLink);
   - target placement: rank 0 packs raw source rows into rank 1's receive
-    slots, rank 1 maps them into its own pool (device-side chunk handshake).
+    slots (staged and moved by the copy engine, or stored straight into the
+    peer slot), rank 1 maps them into its own pool (device-side chunk
+    handshake).
 Rank 1 then maps the same inputs locally; the two pools must be
 bit-identical, untouched rows keeping their canary.
 
@@ -46,6 +48,7 @@ def _worker(rank, port, placement, results):
     import torch.distributed as dist
 
     import cachebridge_b200 as cb
+    from cachebridge_b200.device import status_word
     from cachebridge_b200.online import tp
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -74,26 +77,29 @@ def _worker(rank, port, placement, results):
         if placement == "source":
             peer = tp.exchange_target_pools(plan, target if plan.role == "target" else None, group=host, device=dev)
         else:
+            transport = "peer_stores" if placement == "target_peer_stores" else "copy_engine"
             peer = tp.TargetPlacement(plan, requests, chunk=256, source_layers=L_s, device=dev, group=host,
                                       source_pool=src_pool if plan.role == "source" else None,
                                       mapper=mapper if plan.role == "target" else None,
-                                      target_pool=target if plan.role == "target" else None, timeout_s=20.0)
+                                      target_pool=target if plan.role == "target" else None, timeout_s=20.0,
+                                      transport=transport)
         # Every rank reaches the vote, a local failure included (it votes 0).
         error = None
         ready = torch.ones(1, dtype=torch.int32, device=dev)
         try:
             if placement == "source" and plan.role == "source":
                 tp.ShardedHandoff(mapper, src_pool, peer, requests, chunk=256).run()
-            elif placement == "target":
+            elif placement != "source":
                 for _ in range(2):  # two passes: the slot counters carry over
                     peer.run()
             ready = tp.device_ready(dev)
         except Exception as exc:  # noqa: BLE001
             error = repr(exc)
             ready = torch.zeros(1, dtype=torch.int32, device=dev)
+        bits = int(status_word(dev).item())  # this rank's device status before the vote
         vote = int(tp.publication_vote(ready, device=dev).item())
         if vote != 1:  # not published: every rank stops here
-            results[rank] = (vote, error)
+            results[rank] = (vote, error, bits)
             return
         if plan.role == "target":
             local = cb.TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=dev, fill=CANARY)
@@ -117,7 +123,7 @@ def _worker(rank, port, placement, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("placement", ["source", "target"])
+@pytest.mark.parametrize("placement", ["source", "target", "target_peer_stores"])
 def test_sharded_install_is_bit_exact(placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
