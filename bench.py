@@ -514,7 +514,7 @@ def run_sharded(args):
     if target_side:
         placement = tp.TargetPlacement(plan, requests, chunk=chunk, source_layers=L_s, device=dev, group=host_group,
                                        source_pool=src_pool, mapper=mapper, target_pool=dst_pool,
-                                       transport=args.transport)
+                                       transport=args.transport, slots=args.slots)
         runner = placement
     else:
         peer_pool = tp.exchange_target_pools(plan, dst_pool, group=host_group, device=dev)
@@ -629,6 +629,7 @@ def run_sharded(args):
             config=dict(workload=f"qwen3-14b->32b sharded handoff (BASELINE config 3), TP{plan.tp}+TP{plan.tp}",
                         requests=n_req, request_tokens=n_tok, chunk_tokens=chunk, source_layers=L_s,
                         transport_mode=args.transport if target_side else "peer_stores",
+                        receive_slots=args.slots if target_side else None,
                         target_layers=L_t, kv_heads=H, heads_per_rank=Hr, head_dim=D, selected=S,
                         pool_slots=rows, page_size=1, slot_lists="seeded random", placement=args.placement,
                         transport=transport, l2="inputs larger than L2",
@@ -675,6 +676,7 @@ def main(argv=None):
     ap.add_argument("--request-tokens", type=int, default=32768, help="history tokens per request (N>1)")
     ap.add_argument("--chunk", type=int, default=2048, help="tokens per map+install call (N>1)")
     ap.add_argument("--pool-slack", type=int, default=4096, help="free pool rows beyond the requests (N>1)")
+    ap.add_argument("--slots", type=int, default=2, help="N>1 target placement: receive slots (chunks in flight)")
     ap.add_argument("--transport", choices=["copy_engine", "peer_stores"], default="peer_stores",
                     help="N>1 target placement: staged chunks moved by the copy engine, or gather-kernel peer stores")
     ap.add_argument("--placement", choices=["target", "source"], default="target",

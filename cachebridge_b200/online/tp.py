@@ -277,16 +277,17 @@ class TargetPlacement:
     constructor is collective over ``group`` (all ranks of the world).
     """
 
-    SLOTS = 2
-
     def __init__(self, plan: PairPlan, requests, *, chunk: int, source_layers: int, device: torch.device,
                  group=None, source_pool=None, mapper=None, target_pool=None, timeout_s: float = 10.0,
-                 transport: str = "peer_stores"):
+                 transport: str = "peer_stores", slots: int = 2):
         from .. import _native as nat
         from ..device import storage_dtype_code
 
         if transport not in ("copy_engine", "peer_stores"):
             raise ValueError("transport must be 'copy_engine' or 'peer_stores'")
+        if slots < 2:
+            raise ValueError("target placement needs at least two receive slots")
+        self.SLOTS = slots  # receive slots on the target (chunks in flight)
         self.plan = plan
         self.transport = transport
         self.device = torch.device(device)
@@ -313,14 +314,16 @@ class TargetPlacement:
         uuid = str(torch.cuda.get_device_properties(self.device).uuid)
         if plan.role == "target":
             self.recv = torch.empty((self.SLOTS, slot_elems), dtype=dtype, device=self.device)
-            payload = dict(recv=_export(self.recv), ready=_export(flags), uuid=uuid)
+            payload = dict(recv=_export(self.recv), ready=_export(flags), uuid=uuid, slots=self.SLOTS, chunk=chunk)
         else:
-            payload = dict(consumed=_export(flags), uuid=uuid)
+            payload = dict(consumed=_export(flags), uuid=uuid, slots=self.SLOTS, chunk=chunk)
         self.flags = flags
         torch.cuda.synchronize(self.device)
         gathered = [None] * plan.world
         dist.all_gather_object(gathered, payload, group=group)
         peer = gathered[plan.peer]
+        if (peer["slots"], peer["chunk"]) != (self.SLOTS, chunk):
+            raise ValueError("source and target of a pair must use the same receive slots and chunk size")
         if peer["uuid"] == uuid:
             # The two sides wait on each other's kernels: they must be different GPUs.
             raise ValueError("source and target ranks of a pair share one GPU; target placement needs two")

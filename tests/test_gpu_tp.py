@@ -77,12 +77,13 @@ def _worker(rank, port, placement, results):
         if placement == "source":
             peer = tp.exchange_target_pools(plan, target if plan.role == "target" else None, group=host, device=dev)
         else:
-            transport = "peer_stores" if placement == "target_peer_stores" else "copy_engine"
+            transport = "copy_engine" if placement == "target_copy_engine" else "peer_stores"
+            slots = 3 if placement == "target_3slots" else 2
             peer = tp.TargetPlacement(plan, requests, chunk=256, source_layers=L_s, device=dev, group=host,
                                       source_pool=src_pool if plan.role == "source" else None,
                                       mapper=mapper if plan.role == "target" else None,
                                       target_pool=target if plan.role == "target" else None, timeout_s=20.0,
-                                      transport=transport)
+                                      transport=transport, slots=slots)
         # Every rank reaches the vote, a local failure included (it votes 0).
         error = None
         ready = torch.ones(1, dtype=torch.int32, device=dev)
@@ -123,7 +124,7 @@ def _worker(rank, port, placement, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("placement", ["source", "target", "target_peer_stores"])
+@pytest.mark.parametrize("placement", ["source", "target", "target_copy_engine", "target_3slots"])
 def test_sharded_install_is_bit_exact(placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
