@@ -1,15 +1,15 @@
 #!/usr/bin/env python
 """Benchmark of the CacheBridge online handoff hot path on B200.
 
-Metric (BASELINE.json): mapped+installed KV tokens/s, plus p50 handoff latency
+Metric: mapped+installed KV tokens/s, plus p50 handoff latency
 at an 8K-token history. One "step" is one handoff: every token of the history
 is gathered from the source pool, mapped by the CacheBridge mapper (40 -> 64
 layers, 8 KV heads, S=2) and installed into the target pool rows of its page
 table.
 
-  N=1  (default)  BASELINE config 2: one 8192-token request, page_size=1 pools
+  N=1  (default)  Qwen3-14B->32B shapes on one GPU: one 8192-token request, page_size=1 pools
                   of 262144 slots, seeded random source and target slot lists.
-  N>1  (torchrun) BASELINE config 3 (and its TP2 / TP1 variants): source TP
+  N>1  (torchrun) the sharded handoff (16 x 32768-token requests, at TP4, TP2 or TP1): source TP
                   N/2 + target TP N/2; rank r < N/2 maps its heads for 16 x
                   32768-token requests and stores them straight into the peer
                   target rank's pool (CUDA IPC pointers, NVLink), in
@@ -44,7 +44,7 @@ ROOT = Path(__file__).resolve().parent
 METRIC = "mapped+installed KV tokens/s; p50 handoff latency at 8K-token history"
 UNIT = "tokens/s"
 
-# BASELINE config 2 (Qwen3-14B -> Qwen3-32B shapes)
+# Qwen3-14B -> Qwen3-32B mapper shapes
 QWEN = dict(L_s=40, L_t=64, H=8, D=128, S=2, theta=1e6)
 
 
@@ -318,7 +318,7 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------------------
-# N = 1
+# N = 1: single-GPU handoff of one 8192-token history
 # ----------------------------------------------------------------------------
 def run_single(args):
     import cachebridge_b200 as cb
@@ -459,7 +459,7 @@ def run_single(args):
 
 
 # ----------------------------------------------------------------------------
-# N > 1: BASELINE config 3 (source TP N/2 + target TP N/2, peer stores)
+# N > 1: sharded handoff (source TP N/2 + target TP N/2 over NVLink)
 # ----------------------------------------------------------------------------
 def run_sharded(args):
     import datetime

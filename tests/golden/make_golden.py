@@ -10,7 +10,7 @@ reference's ``layer_NNN.safetensors`` format, ``case.safetensors`` (inputs and
 the reference's outputs) and ``case.json`` (call parameters). The reference is
 not needed afterwards: tests read only the committed fixtures.
 
-Inputs are seeded synthetic tensors shaped like BASELINE.json's configurations
+Inputs are seeded synthetic tensors shaped like the benchmark configurations
 (reduced token / layer counts so fixtures stay small) plus re-creations of the
 inputs of the reference's own known-answer tests (tests/test_mapper.py,
 tests/test_fitting.py, tests/test_blocks.py, examples/fit_and_map.py).
@@ -314,18 +314,18 @@ def main(argv):
     fit_cases(ref)
     pack_case(ref)
     geometry_case(ref)
-    # BASELINE config 1 (CPU toy, fp32): 4 -> 6 layers, 2 heads x 64, S=2, 1024-slot pool at a
+    # CPU toy configuration (fp32): 4 -> 6 layers, 2 heads x 64, S=2, 1024-slot pool at a
     # seeded random permutation (128 of the config's 512 tokens, to keep the fixture small).
     random_case(ref, "cfg1_toy", seed=1, L_s=4, L_t=6, H=2, D=64, S=2, n=128, dtype=torch.float32,
                 position_start=0, source_theta=1e6, target_theta=1e6, w_var=1 / 128, b_var=0.01,
                 pool_rows=1024)
-    # BASELINE config 2 shapes, reduced: bf16, head_dim 128, per-channel LogNormal scales,
+    # Qwen3-14B -> 32B shapes, reduced: bf16, head_dim 128, per-channel LogNormal scales,
     # TP rank 1 of 2 narrowed from a full 4-head page, large absolute positions.
     random_case(ref, "qwen_mini_bf16", seed=2, L_s=6, L_t=4, H=2, D=128, S=2, n=130,
                 dtype=torch.bfloat16, position_start=1000, source_theta=1e6, target_theta=1e6,
                 tp_rank=1, tp_size=2, w_var=1 / 256, lognormal=True, bf16_weights=True,
                 pool_rows=4096)
-    # BASELINE config 4 shapes, reduced: S=4 (512 x 128 maps), Llama theta.
+    # Llama-3.1-8B -> 70B shapes, reduced: S=4 (512 x 128 maps), Llama theta.
     random_case(ref, "llama_mini_s4", seed=4, L_s=6, L_t=2, H=2, D=128, S=4, n=130,
                 dtype=torch.bfloat16, position_start=16384, source_theta=5e5, target_theta=5e5,
                 w_var=1 / 512, lognormal=True, bf16_weights=True, pool_rows=2048)

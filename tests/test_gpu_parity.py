@@ -171,9 +171,9 @@ def _check_install(pool, loc, expected_f32, *, dtype, head_offset=0, heads=None)
 @pytest.mark.parametrize(
     "L_s,L_t,H,D,S,n,dtype",
     [
-        (4, 6, 2, 64, 2, 512, torch.float32),     # BASELINE config 1 (toy, fp32)
-        (40, 64, 8, 128, 2, 600, torch.bfloat16),  # config 2 shapes, partial m-tile
-        (32, 80, 8, 128, 4, 257, torch.bfloat16),  # config 4 shapes (S=4)
+        (4, 6, 2, 64, 2, 512, torch.float32),     # CPU toy configuration (fp32)
+        (40, 64, 8, 128, 2, 600, torch.bfloat16),  # Qwen3-14B -> 32B shapes, partial m-tile
+        (32, 80, 8, 128, 4, 257, torch.bfloat16),  # Llama-3.1-8B -> 70B shapes (S=4)
         (12, 5, 2, 128, 1, 129, torch.bfloat16),
         (12, 4, 2, 128, 3, 1, torch.bfloat16),
         (12, 3, 2, 128, 5, 300, torch.bfloat16),   # streamed weights (S > 4)
@@ -382,7 +382,7 @@ def test_target_rope_at_far_positions(tmp_path, cuda_device, start):
 
 
 def test_config2_full_size_properties(tmp_path, cuda_device):
-    """BASELINE config 2 shapes at the full 8192-token history: every target
+    """Qwen3-14B -> 32B shapes at the full 8192-token history: every target
     row lands at its slot and nothing else changes (bit-exact), and a token
     window of every layer and head matches the oracle within the BF16 bound."""
     g = torch.Generator().manual_seed(2024)

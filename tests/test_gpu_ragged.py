@@ -1,4 +1,4 @@
-"""Ragged serving batch (reduced sizes) on one GPU.
+"""Ragged serving batch (the ragged TP4 configuration, reduced sizes) on one GPU.
 
 A target pool is 70 % occupied by other requests' rows (seeded random
 allocation). Twelve requests with LogNormal history lengths are installed
@@ -9,8 +9,8 @@ free rows. Checked:
     evaluation of its whole sequence within the BF16 bound;
   - occupied rows keep their bytes and never-allocated rows keep the canary
     (bit-exact).
-Lengths are LogNormal(ln 384, 1.0) clipped to [32, 2048] (config 5 uses
-ln 4096 and [256, 32768]); the suffix is 96 tokens (config 5: 1024).
+Lengths are LogNormal(ln 384, 1.0) clipped to [32, 2048] (the full
+configuration uses ln 4096 and [256, 32768]); the suffix is 96 tokens (full: 1024).
 """
 
 from __future__ import annotations
