@@ -126,41 +126,75 @@ __global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 // Row copies (gather / scatter)
 // ---------------------------------------------------------------------------
-// One warp per (kind, layer, token) row; VEC-byte vectors across lanes.
-template <typename V>
+// Warps walk groups of RPW consecutive tokens of one (kind, layer); V-byte
+// vectors across lanes. Short rows (one vector per lane or less) take RPW = 4
+// so each lane keeps four independent loads in flight and the (kind, layer,
+// token) decomposition is paid once per group; longer rows take RPW = 1 and
+// loop over their vectors.
+template <typename V, int RPW>
 __global__ void __launch_bounds__(256) copy_rows_kernel(const __grid_constant__ CopyRowsParams p) {
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t rows_total = 2 * static_cast<int64_t>(p.layers) * p.n;
+  const int64_t groups_per_kl = (p.n + RPW - 1) / RPW;
+  const int64_t groups_total = 2 * static_cast<int64_t>(p.layers) * groups_per_kl;
   const int lane = threadIdx.x & 31;
   const int nvec = p.row_bytes / static_cast<int>(sizeof(V));
   for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-       w < rows_total; w += warps_total) {
-    const int64_t t = w % p.n;
-    const int64_t kl = w / p.n;
+       w < groups_total; w += warps_total) {
+    const int64_t kl = w / groups_per_kl;
+    const int64_t t0 = (w - kl * groups_per_kl) * RPW;
     const int layer = static_cast<int>(kl % p.layers);
     const int kind = static_cast<int>(kl / p.layers);
-    const int64_t ss = load_slot(p.src_slots, p.src_slot_dtype, t);
-    const int64_t ds = load_slot(p.dst_slots, p.dst_slot_dtype, t);
-    if (ss < 0 || ss >= p.src_rows || ds < 0 || ds >= p.dst_rows) {
-      if (lane == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-      continue;
+    const char* src_base = reinterpret_cast<const char*>(kind ? p.src_v[layer] : p.src_k[layer]) + p.src_offset_bytes;
+    char* dst_base = reinterpret_cast<char*>(kind ? p.dst_v[layer] : p.dst_k[layer]) + p.dst_offset_bytes;
+    const char* src[RPW];
+    char* dst[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      src[r] = nullptr;
+      dst[r] = nullptr;
+      const int64_t t = t0 + r;
+      if (t >= p.n) continue;
+      const int64_t ss = load_slot(p.src_slots, p.src_slot_dtype, t);
+      const int64_t ds = load_slot(p.dst_slots, p.dst_slot_dtype, t);
+      if (ss < 0 || ss >= p.src_rows || ds < 0 || ds >= p.dst_rows) {
+        if (lane == 0) flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+        continue;
+      }
+      src[r] = src_base + ss * p.src_stride_bytes;
+      dst[r] = dst_base + ds * p.dst_stride_bytes;
     }
-    const char* src = reinterpret_cast<const char*>(kind ? p.src_v[layer] : p.src_k[layer]) +
-                      ss * p.src_stride_bytes + p.src_offset_bytes;
-    char* dst = reinterpret_cast<char*>(kind ? p.dst_v[layer] : p.dst_k[layer]) +
-                ds * p.dst_stride_bytes + p.dst_offset_bytes;
-    for (int e = lane; e < nvec; e += 32) {
-      reinterpret_cast<V*>(dst)[e] = reinterpret_cast<const V*>(src)[e];
+    if (RPW > 1) {
+      V v[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+        if (src[r] != nullptr && lane < nvec) v[r] = reinterpret_cast<const V*>(src[r])[lane];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
+        if (src[r] != nullptr && lane < nvec) reinterpret_cast<V*>(dst[r])[lane] = v[r];
+    } else {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        if (src[r] == nullptr) continue;
+        for (int e = lane; e < nvec; e += 32) reinterpret_cast<V*>(dst[r])[e] = reinterpret_cast<const V*>(src[r])[e];
+      }
     }
   }
 }
 
+template <typename V>
+static void copy_rows_dispatch(const CopyRowsParams& p, int blocks, cudaStream_t st) {
+  if (p.row_bytes <= 32 * static_cast<int>(sizeof(V)))
+    copy_rows_kernel<V, 4><<<blocks, 256, 0, st>>>(p);
+  else
+    copy_rows_kernel<V, 1><<<blocks, 256, 0, st>>>(p);
+}
+
 cudaError_t launch_copy_rows(int vec_bytes, const CopyRowsParams& p, int blocks, cudaStream_t st) {
   switch (vec_bytes) {
-    case 16: copy_rows_kernel<uint4><<<blocks, 256, 0, st>>>(p); break;
-    case 8: copy_rows_kernel<uint2><<<blocks, 256, 0, st>>>(p); break;
-    case 4: copy_rows_kernel<uint32_t><<<blocks, 256, 0, st>>>(p); break;
-    default: copy_rows_kernel<uint16_t><<<blocks, 256, 0, st>>>(p); break;
+    case 16: copy_rows_dispatch<uint4>(p, blocks, st); break;
+    case 8: copy_rows_dispatch<uint2>(p, blocks, st); break;
+    case 4: copy_rows_dispatch<uint32_t>(p, blocks, st); break;
+    default: copy_rows_dispatch<uint16_t>(p, blocks, st); break;
   }
   return cudaGetLastError();
 }
