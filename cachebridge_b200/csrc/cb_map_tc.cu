@@ -27,8 +27,8 @@
 //               n with n % 3 == g (TMEM accumulator n % 4). In a
 //               group, warp w reads TMEM lane quarter w % 4 (token rows, one
 //               per thread), in four rounds of 16 RoPE pairs (columns i and
-//               i+64): target RoPE for keys (coefficients from a table-driven
-//               sin/cos of the exact FP32 phase), BF16 packing, a swizzled
+//               i+64): target RoPE for keys (sin/cos of the exact FP32 phase
+//               after a Cody-Waite reduction by pi), BF16 packing, a swizzled
 //               32 x 64 B staging tile, then 16-byte stores of 8 rows x
 //               (2 x 32 B) per warp instruction.
 //   warp 16     TMEM owner + single-thread tcgen05.mma issuer: per m-tile one
@@ -41,6 +41,8 @@
 //               per m-tile otherwise.
 // Every wait is bounded (kWaitTimeoutNs): an expired wait flags
 // CB_DEV_ERR_TIMEOUT and the CTA unwinds instead of hanging.
+#include <climits>
+
 #include "cb_device.cuh"
 #include "cb_map_tc.cuh"
 
@@ -109,29 +111,49 @@ __device__ __forceinline__ uint64_t make_noswizzle_k16_desc(uint32_t smem_addr) 
   return d;  // layout type 0: no swizzle
 }
 
-// cos and sin of an FP32 phase: Cody-Waite reduction by pi/2
-// (k = rint(phi * 2/pi); r = phi - k*C1 - k*C2 with C1 = fl(pi/2) and
-// C2 = fl(pi/2 - C1), each product exact inside the FMA), the hardware
-// sin/cos approximations on |r| <= pi/4 (__sincosf: absolute error below
-// 2^-21 on [-pi, pi]), then the quadrant k mod 4 swaps and negates. Within
-// 4e-7 of cos/sin(phi) for |phi| < 4e5 (k stays an exact FP32 integer),
-// far below the BF16 rounding of the output; calls with larger phases use
-// sincosf (MapTcParams::trig_exact). Few issue slots and no shared memory:
-// the epilogue warps share their schedulers with the MMA issuer.
-__device__ __forceinline__ void sincos_reduced(float phi, float& c, float& s) {
-  const float kTwoOverPi = 0x1.45f306p-1f;  // fl(2 / pi)
-  const float kC1 = 0x1.921fb6p+0f;         // fl(pi / 2)
-  const float kC2 = -0x1.777a5cp-25f;       // fl(pi / 2 - kC1)
-  const float kf = rintf(phi * kTwoOverPi);
-  float r = fmaf(-kf, kC1, phi);
-  r = fmaf(-kf, kC2, r);
-  float sr, cr;
-  __sincosf(r, &sr, &cr);
-  const int q = static_cast<int>(kf) & 3;
-  const float a = (q & 1) ? cr : sr;  // sin(phi) before the sign
-  const float b = (q & 1) ? sr : cr;  // cos(phi) before the sign
-  s = (q & 2) ? -a : a;
-  c = ((q + 1) & 2) ? -b : b;
+// cos and sin of an FP32 phase up to a sign: Cody-Waite reduction by pi
+// (k = rint(phi / pi); r = phi - k*P1 - k*P2 with P1 = fl(pi) and
+// P2 = fl(pi - P1); phi - k*P1 is exact inside the FMA), then the hardware
+// sin/cos approximations on |r| <= pi/2 (__sincosf: absolute error below
+// 2^-21 on [-pi, pi]). cos(phi) = (-1)^k cos(r) and sin(phi) = (-1)^k sin(r);
+// `sign` is (-1)^k as an FP32 sign-bit mask, applied by the caller to the
+// rotated pair. Within 4e-7 of cos/sin(phi) for |phi| < 4e5 (k stays an exact
+// FP32 integer), far below the BF16 rounding of the output; calls with larger
+// phases use sincosf (MapTcParams::trig_exact). Few issue slots and no shared
+// memory: the epilogue warps share their schedulers with the MMA issuer.
+__device__ __forceinline__ void sincos_half_turns(float phi, float& c, float& s, uint32_t& sign) {
+  const float kOneOverPi = 0x1.45f306p-2f;  // fl(1 / pi)
+  const float kP1 = 0x1.921fb6p+1f;         // fl(pi)
+  const float kP2 = -0x1.777a5cp-24f;       // fl(pi - kP1)
+  const float kf = rintf(phi * kOneOverPi);
+  float r = fmaf(-kf, kP1, phi);
+  r = fmaf(-kf, kP2, r);
+  __sincosf(r, &s, &c);
+  sign = static_cast<uint32_t>(static_cast<int>(kf)) << 31;
+}
+
+// Token lookups. A row's token is token_order[t] (or t) for processing index
+// t; the producers and the epilogue read the order entry two m-tiles ahead
+// and the slot one m-tile ahead, so neither dependent load stalls a pipeline
+// role. kNoToken marks a row past the call's (or item's) end.
+constexpr int kNoToken = INT_MIN;
+
+__device__ __forceinline__ int item_token_raw(const MapTcParams& p, const Item& it, int mm, int row) {
+  if (mm >= it.mtiles) return kNoToken;
+  const int t = it.tok0 + mm * kBM + row;
+  if (t >= p.n_tokens) return kNoToken;
+  return p.order == nullptr ? t : __ldg(p.order + t);
+}
+
+// A token read by item_token_raw, or -1 for none. An order entry outside
+// [0, n) flags CB_DEV_ERR_SLOT_RANGE and the row is skipped.
+__device__ __forceinline__ int check_token(const MapTcParams& p, int raw) {
+  if (raw == kNoToken) return -1;
+  if (raw < 0 || raw >= p.n_tokens) {
+    flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+    return -1;
+  }
+  return raw;
 }
 
 // ------------------------------- producers ---------------------------------
@@ -150,29 +172,24 @@ __device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int la
   bool ok = true;
   for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
     const Item it = decode_item(p, i);
-    // Source slot of this lane's row (processing index next_t holds token
-    // p.order[next_t]), prefetched one m-tile ahead (values only).
-    int next_t = it.tok0 + pw * 32 + lane;
-    int next_valid = 0;
-    int64_t next_row = 0;
-    if (it.kind == 1 && next_t < p.n_tokens) {
-      const int tok = token_at(p.order, next_t, p.n_tokens, p.status);
-      next_valid = tok >= 0;
-      if (next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, tok);
+    // Source slot of this lane's row (values only): tok_c / row_c for m-tile
+    // m, raw_n the order entry of m-tile m + 1.
+    const int row_in_tile = pw * 32 + lane;
+    int tok_c = -1, raw_n = kNoToken;
+    int64_t row_c = 0;
+    if (it.kind == 1) {
+      tok_c = check_token(p, item_token_raw(p, it, 0, row_in_tile));
+      if (tok_c >= 0) row_c = load_slot(p.src_slots, p.src_slot_dtype, tok_c);
+      raw_n = item_token_raw(p, it, 1, row_in_tile);
     }
     for (int m = 0; m < it.mtiles && ok; ++m) {
       const int tok0 = it.tok0 + m * kBM;
-      int valid = next_valid;
-      int64_t srow = next_row;
-      if (m + 1 < it.mtiles) {
-        next_t += kBM;
-        next_valid = 0;
-        next_row = 0;
-        if (it.kind == 1 && next_t < p.n_tokens) {
-          const int tok = token_at(p.order, next_t, p.n_tokens, p.status);
-          next_valid = tok >= 0;
-          if (next_valid) next_row = load_slot(p.src_slots, p.src_slot_dtype, tok);
-        }
+      int valid = tok_c >= 0;
+      const int64_t srow = row_c;
+      if (it.kind == 1) {
+        tok_c = check_token(p, raw_n);
+        row_c = tok_c >= 0 ? load_slot(p.src_slots, p.src_slot_dtype, tok_c) : 0;
+        raw_n = item_token_raw(p, it, m + 2, row_in_tile);
       }
       if (it.kind == 1 && valid && (srow < 0 || srow >= p.src_rows)) {
         flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
@@ -387,101 +404,144 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
   return r;
 }
 
-// Warp (group g, lane quarter eq): the m-tiles n with n % 4 == g, token rows
-// eq*32 + lane (one per thread), accumulator g.
+// One m-tile of an epilogue group: item index i (decoded in it), m-tile m of
+// the item, CTA m-tile counter n.
+struct TileCursor {
+  int i, m, n;
+  Item it;
+};
+
+// Moves c forward by `step` m-tiles of the CTA's sequence, across items.
+__device__ __forceinline__ void cursor_advance(const MapTcParams& p, TileCursor& c, int step) {
+  c.m += step;
+  c.n += step;
+  while (c.i < p.num_items && c.m >= c.it.mtiles) {
+    c.m -= c.it.mtiles;
+    c.i += gridDim.x;
+    if (c.i < p.num_items) c.it = decode_item(p, c.i);
+  }
+}
+
+__device__ __forceinline__ int cursor_token_raw(const MapTcParams& p, const TileCursor& c, int row) {
+  return c.i < p.num_items ? item_token_raw(p, c.it, c.m, row) : kNoToken;
+}
+
+// Warp (group g, lane quarter eq): the m-tiles n with n % 3 == g, token rows
+// eq*32 + lane (one per thread), accumulator n % 4. The destination slot of
+// the next m-tile is loaded while this one is processed.
 __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int g, int eq, int lane) {
   uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 64 B, this warp only
   uint8_t* my_row = stage + lane * 64;
   const int my_key = (lane >> 1) & 3;  // staging swizzle of this lane's row
   const int64_t dst_stride_bytes = p.dst_row_stride * 2;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eq * 32) << 16);
-  int n = 0;  // CTA m-tile counter
-  bool ok = true;
-  for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
-    const Item it = decode_item(p, i);
-    char* dst_layer = reinterpret_cast<char*>(it.kind ? p.dst_v[it.l] : p.dst_k[it.l]) +
-                      static_cast<int64_t>(p.dst_head_offset + it.h) * (kD * 2);
-    for (int m = 0; m < it.mtiles; ++m, ++n) {
-      if (n % kEpiGroups != g) continue;
-      const int acc = n & 3;  // accumulator buffer of this m-tile
-      const uint32_t tbase = lane_base + acc * kD;
-      const int t = it.tok0 + m * kBM + eq * 32 + lane;
-      char* row_ptr = nullptr;  // this lane's destination row, or null
-      int tok = -1;  // the token at processing index t
-      if (t < p.n_tokens) tok = token_at(p.order, t, p.n_tokens, p.status);
-      if (tok >= 0) {
-        const int64_t slot = load_slot(p.dst_slots, p.dst_slot_dtype, tok);
-        if (slot < 0 || slot >= p.dst_rows)
-          flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-        else
-          row_ptr = dst_layer + slot * dst_stride_bytes;
-      }
-      const bool do_rope = it.kind == 0 && row_ptr != nullptr;
-      const float pos = static_cast<float>(p.position_start + (tok < 0 ? 0 : tok));
-      // Warp-uniform outcome: tcgen05.ld is .sync.aligned across the warp.
-      const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (n >> 2) & 1, s.abort_flag, p.status);
-      if (!__all_sync(0xffffffffu, got)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+  const int row_in_tile = eq * 32 + lane;
+  TileCursor cur;
+  cur.i = blockIdx.x;
+  cur.m = 0;
+  cur.n = 0;
+  if (cur.i < p.num_items) cur.it = decode_item(p, cur.i);
+  cursor_advance(p, cur, g);
+  TileCursor nxt = cur;
+  cursor_advance(p, nxt, kEpiGroups);
+  int tok = check_token(p, cursor_token_raw(p, cur, row_in_tile));
+  int64_t slot = tok >= 0 ? load_slot(p.dst_slots, p.dst_slot_dtype, tok) : 0;
+  int raw_nxt = cursor_token_raw(p, nxt, row_in_tile);
+  while (cur.i < p.num_items) {
+    TileCursor after = nxt;
+    cursor_advance(p, after, kEpiGroups);
+    const int tok_nxt = check_token(p, raw_nxt);
+    const int64_t slot_nxt = tok_nxt >= 0 ? load_slot(p.dst_slots, p.dst_slot_dtype, tok_nxt) : 0;
+    raw_nxt = cursor_token_raw(p, after, row_in_tile);
+
+    const Item& it = cur.it;
+    const int n = cur.n;
+    const int acc = n & 3;  // accumulator buffer of this m-tile
+    const uint32_t tbase = lane_base + acc * kD;
+    char* row_ptr = nullptr;  // this lane's destination row, or null
+    if (tok >= 0) {
+      if (slot < 0 || slot >= p.dst_rows)
+        flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
+      else
+        row_ptr = reinterpret_cast<char*>(it.kind ? p.dst_v[it.l] : p.dst_k[it.l]) +
+                  static_cast<int64_t>(p.dst_head_offset + it.h) * (kD * 2) + slot * dst_stride_bytes;
+    }
+    const bool do_rope = it.kind == 0 && row_ptr != nullptr;
+    const float pos = static_cast<float>(p.position_start + (tok < 0 ? 0 : tok));
+    // Warp-uniform outcome: tcgen05.ld is .sync.aligned across the warp.
+    const bool got = mbar_wait(bar_at(s, kBarAccFull + acc), (n >> 2) & 1, s.abort_flag, p.status);
+    if (!__all_sync(0xffffffffu, got)) break;
+    tc_fence_after();
 #pragma unroll 1
-      for (int r = 0; r < 4; ++r) {  // RoPE pairs [16r, 16r + 16)
-        const int p0 = 16 * r;
-        uint32_t lo[16], hi[16];
-        tmem_ld_32x32b_x16(tbase + p0, lo);
-        tmem_ld_32x32b_x16(tbase + 64 + p0, hi);
-        tmem_wait_ld();
-        if (r == 3) {
-          // Accumulator fully read into registers: hand it back to the MMA.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
+    for (int r = 0; r < 4; ++r) {  // RoPE pairs [16r, 16r + 16)
+      const int p0 = 16 * r;
+      uint32_t lo[16], hi[16];
+      tmem_ld_32x32b_x16(tbase + p0, lo);
+      tmem_ld_32x32b_x16(tbase + 64 + p0, hi);
+      tmem_wait_ld();
+      if (r == 3) {
+        // Accumulator fully read into registers: hand it back to the MMA.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_at(s, kBarAccEmpty + acc));
+      }
+      float ylo[16], yhi[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        ylo[e] = __uint_as_float(lo[e]);
+        yhi[e] = __uint_as_float(hi[e]);
+      }
+      if (do_rope && p.trig_exact) {
+        for (int e = 0; e < 16; ++e) {
+          float c, sn, o0, o1;
+          sincosf(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), &sn, &c);
+          rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
+          ylo[e] = o0;
+          yhi[e] = o1;
         }
-        float ylo[16], yhi[16];
+      } else if (do_rope) {
+        // (y_lo + i y_hi) * (cos r + i sin r), then the sign (-1)^k.
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          ylo[e] = __uint_as_float(lo[e]);
-          yhi[e] = __uint_as_float(hi[e]);
+          float c, sn;
+          uint32_t sg;
+          sincos_half_turns(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), c, sn, sg);
+          const float o0 = fmaf(ylo[e], c, -__fmul_rn(yhi[e], sn));
+          const float o1 = fmaf(yhi[e], c, __fmul_rn(ylo[e], sn));
+          ylo[e] = __uint_as_float(__float_as_uint(o0) ^ sg);
+          yhi[e] = __uint_as_float(__float_as_uint(o1) ^ sg);
         }
-        if (do_rope && p.trig_exact) {
-          for (int e = 0; e < 16; ++e) {
-            float c, sn, o0, o1;
-            sincosf(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), &sn, &c);
-            rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
-            ylo[e] = o0;
-            yhi[e] = o1;
-          }
-        } else if (do_rope) {
+        if (p.dst_magnitude != 1.0f) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            float c, sn, o0, o1;
-            sincos_reduced(__fmul_rn(pos, p.dst_inv_freq[p0 + e]), c, sn);
-            rope_apply_pair(ylo[e], yhi[e], __fmul_rn(c, p.dst_magnitude), __fmul_rn(sn, p.dst_magnitude), o0, o1);
-            ylo[e] = o0;
-            yhi[e] = o1;
+            ylo[e] = __fmul_rn(ylo[e], p.dst_magnitude);
+            yhi[e] = __fmul_rn(yhi[e], p.dst_magnitude);
           }
         }
-        // Local chunk lc of the round's 64-byte row piece (0-1: columns
-        // [p0, p0+16), 2-3: [64+p0, ...)) sits at lc ^ ((row >> 1) & 3).
-        *reinterpret_cast<uint4*>(my_row + ((0 ^ my_key) << 4)) = pack8(ylo);
-        *reinterpret_cast<uint4*>(my_row + ((1 ^ my_key) << 4)) = pack8(ylo + 8);
-        *reinterpret_cast<uint4*>(my_row + ((2 ^ my_key) << 4)) = pack8(yhi);
-        *reinterpret_cast<uint4*>(my_row + ((3 ^ my_key) << 4)) = pack8(yhi + 8);
-        __syncwarp();
-        // Stores: 8 rows x (2 x 32 contiguous bytes) per warp instruction.
-        const int lc = lane & 3;
-        const int gchunk = lc < 2 ? 2 * r + lc : 8 + 2 * r + (lc - 2);
-#pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
-          const int rr = 8 * qq + (lane >> 2);
-          char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((lc ^ ((rr >> 1) & 3)) << 4));
-          if (dst != nullptr) *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
-        }
-        __syncwarp();
       }
+      // Local chunk lc of the round's 64-byte row piece (0-1: columns
+      // [p0, p0+16), 2-3: [64+p0, ...)) sits at lc ^ ((row >> 1) & 3).
+      *reinterpret_cast<uint4*>(my_row + ((0 ^ my_key) << 4)) = pack8(ylo);
+      *reinterpret_cast<uint4*>(my_row + ((1 ^ my_key) << 4)) = pack8(ylo + 8);
+      *reinterpret_cast<uint4*>(my_row + ((2 ^ my_key) << 4)) = pack8(yhi);
+      *reinterpret_cast<uint4*>(my_row + ((3 ^ my_key) << 4)) = pack8(yhi + 8);
+      __syncwarp();
+      // Stores: 8 rows x (2 x 32 contiguous bytes) per warp instruction.
+      const int lc = lane & 3;
+      const int gchunk = lc < 2 ? 2 * r + lc : 8 + 2 * r + (lc - 2);
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        const int rr = 8 * qq + (lane >> 2);
+        char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((lc ^ ((rr >> 1) & 3)) << 4));
+        if (dst != nullptr) *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
+      }
+      __syncwarp();
     }
+    cur = nxt;
+    nxt = after;
+    tok = tok_nxt;
+    slot = slot_nxt;
   }
 }
 
