@@ -9,7 +9,7 @@ interface. GPU kernels are reached through the C ABI in
 from .device import RowSet, raise_for_status, read_status
 from .install import DirectMappedPoolCodec, contiguous_runs
 from .mapper import LayerWeights, PageMapper
-from .pool import TokenKVPool
+from .pool import TokenKVPool, token_slots_from_pages
 
 __all__ = [
     "DirectMappedPoolCodec",
@@ -20,4 +20,5 @@ __all__ = [
     "contiguous_runs",
     "raise_for_status",
     "read_status",
+    "token_slots_from_pages",
 ]

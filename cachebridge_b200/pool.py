@@ -57,3 +57,30 @@ class TokenKVPool:
     def rows(self, slots: torch.Tensor | None = None, head_offset: int = 0) -> RowSet:
         """C-ABI row-set view of this pool addressed through ``slots``."""
         return RowSet.from_pool(self, slots, head_offset)
+
+
+def token_slots_from_pages(page_table, page_size: int, n_tokens: int | None = None) -> torch.Tensor:
+    """Token slots of a request held in pages of ``page_size`` tokens.
+
+    A paged SGLang pool still stores one row per token: token i of the request
+    sits at row ``page_table[i // page_size] * page_size + i % page_size``
+    (the ``req_to_token`` row the reference's adapter reads as
+    ``device_indices``, backends/sglang/runtime/clean_adapter.py:370-380). The
+    history must be non-empty and page-aligned, as the reference requires.
+    Returns int64 slots on the page table's device.
+    """
+    pages = torch.as_tensor(page_table)
+    if type(page_size) is not int or page_size <= 0:
+        raise ValueError("page_size must be a positive integer")
+    if pages.ndim != 1 or pages.dtype not in (torch.int32, torch.int64):
+        raise ValueError("page_table must be a 1-D integer tensor")
+    n = pages.numel() * page_size if n_tokens is None else int(n_tokens)
+    if n == 0 or n % page_size:
+        raise ValueError("Only nonempty page-aligned histories supported")
+    if n > pages.numel() * page_size:
+        raise ValueError("page_table holds fewer tokens than requested")
+    used = pages[: n // page_size].long()
+    if bool((used < 0).any()):
+        raise ValueError("negative page index")
+    offsets = torch.arange(page_size, device=used.device, dtype=torch.int64)
+    return (used.unsqueeze(1) * page_size + offsets).reshape(-1)
