@@ -97,6 +97,21 @@ int ensure_access(int device, const void* ptr, const char* what) {
 
 // Peer access for the first K and V buffers of a row set (the layers of one
 // row set share a device).
+// True when the row set's buffers are memory of `device` itself rather than a
+// peer GPU's mapping. A row set's layers share one device (the same rule as
+// ensure_rows_access), so layer 0's K and V buffers decide.
+bool rows_on_device(int device, const cb_rows* r) {
+  for (const void* ptr : {static_cast<const void*>(r->k[0]), static_cast<const void*>(r->v[0])}) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (a.type != cudaMemoryTypeDevice || a.device != device) return false;
+  }
+  return true;
+}
+
 int ensure_rows_access(int device, const cb_rows* r, const char* what) {
   int rc = ensure_access(device, r->k[0], what);
   if (rc != CB_OK) return rc;
@@ -325,6 +340,7 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.dst_head_offset = dst->head_offset;
   p.dst_slot_dtype = dst->slot_dtype;
   p.dst_slots = dst->slots;
+  p.dst_evict_first = rows_on_device(m->device, dst) ? 1 : 0;
   std::memcpy(p.dst_inv_freq, dst_rope->inv_freq, sizeof(p.dst_inv_freq));
   p.dst_magnitude = dst_rope->magnitude;
   p.position_start = position_start;

@@ -30,8 +30,9 @@
 //               i+64): target RoPE for keys (sin/cos of the exact FP32 phase
 //               after a Cody-Waite reduction by pi), BF16 packing, a swizzled
 //               32 x 64 B staging tile, then 16-byte stores of 8 rows x
-//               (2 x 32 B) per warp instruction, with an L2 evict-first
-//               policy so the stores do not push shared source rows out.
+//               (2 x 32 B) per warp instruction; into this GPU's own pool
+//               with an L2 evict-first policy, so the stores do not push
+//               shared source rows out.
 //   warp 16     TMEM owner + single-thread tcgen05.mma issuer: per m-tile one
 //               K=16 step that loads the bias (a constant ones column times a
 //               [bias_hi, bias_lo] block), then 8 K=16 steps per 128-feature
@@ -536,7 +537,12 @@ __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_
         const int rr = 8 * qq + (lane >> 2);
         char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
         const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((lc ^ ((rr >> 1) & 3)) << 4));
-        if (dst != nullptr) st_global_v4_hint(dst + gchunk * 16, v, store_policy);
+        if (dst != nullptr) {
+          if (p.dst_evict_first)
+            st_global_v4_hint(dst + gchunk * 16, v, store_policy);
+          else
+            *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
+        }
       }
       __syncwarp();
     }

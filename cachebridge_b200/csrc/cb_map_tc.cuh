@@ -60,6 +60,8 @@ struct MapTcParams {
   int dst_head_offset;
   int dst_slot_dtype;
   const void* dst_slots;
+  int dst_evict_first;      // 1: the target rows are this GPU's memory; store them with an
+                            // L2 evict-first policy (peer pools get plain stores)
 
   float dst_inv_freq[64];   // target RoPE
   float dst_magnitude;
