@@ -237,6 +237,87 @@ def reprefill_estimate(device, *, tokens, requests, tp, reps=3):
 
 
 # ----------------------------------------------------------------------------
+# The reference's torch path on this GPU (the baseline the fused kernels replace)
+# ----------------------------------------------------------------------------
+def torch_reference_handoff(layers, src_pool, src_slots, dst_pool, dst_slots, *, theta, position_start=0):
+    """One handoff the way the reference runs it with torch on a GPU.
+
+    pack_source_block: one index_select per source layer and kind into a
+    [2, L_s, n, H, D] block (online/blocks.py:47-82). PageMapper.map_page in
+    FP32: RoPE removed from the keys of every source layer,
+    (x*cos - rot(x)*sin) / max(cos^2 + sin^2, tiny) (rope.py:82-89); per target
+    layer the selected layers concatenated along features and
+    einsum('thf,hfd->thd') with the FP32 weights plus bias (mapper.py:153-181);
+    target RoPE on the keys and the cast to the pool dtype (mapper.py:207-239).
+    Install: k_buffer[l][loc] = k per target layer (SGLang set_kv_buffer,
+    blocks.py:86-111). Returns the mapped [2, L_t, n, H, D] block.
+    """
+    dev = src_pool.k_buffer.device
+    n = len(src_slots)
+    L_s, H, D = src_pool.layer_num, src_pool.heads, src_pool.head_dim
+    block = torch.empty((2, L_s, n, H, D), dtype=src_pool.dtype, device=dev)
+    for l in range(L_s):
+        torch.index_select(src_pool.k_buffer[l], 0, src_slots, out=block[0, l])
+        torch.index_select(src_pool.v_buffer[l], 0, src_slots, out=block[1, l])
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, device=dev).float() / D))
+    phase = (torch.arange(n, device=dev) + position_start).float()[:, None] * inv[None, :]
+    phase = torch.cat((phase, phase), dim=-1)
+    cos, sin = phase.cos()[None, :, None, :], phase.sin()[None, :, None, :]
+
+    def rot(x):
+        a, b = x.chunk(2, dim=-1)
+        return torch.cat((-b, a), dim=-1)
+
+    keys = block[0].float()
+    keys = (keys * cos - rot(keys) * sin) / torch.clamp_min(cos * cos + sin * sin, torch.finfo(torch.float32).tiny)
+    values = block[1].float()
+    out_k, out_v = [], []
+    for t in layers:
+        sel = t["selected"].tolist()
+        xk = torch.cat([keys[s] for s in sel], dim=-1)
+        xv = torch.cat([values[s] for s in sel], dim=-1)
+        out_k.append(torch.einsum("thf,hfd->thd", xk, t["k_weight"]) + t["k_bias"])
+        out_v.append(torch.einsum("thf,hfd->thd", xv, t["v_weight"]) + t["v_bias"])
+    k = torch.stack(out_k)
+    k = k * cos + rot(k) * sin
+    mapped = torch.stack((k, torch.stack(out_v))).to(dst_pool.dtype)
+    for l in range(dst_pool.layer_num):
+        dst_pool.k_buffer[l][dst_slots] = mapped[0, l]
+        dst_pool.v_buffer[l][dst_slots] = mapped[1, l]
+    return mapped
+
+
+def torch_reference_timing(layers, src_pool, src_slots, dst_pool, dst_slots, *, theta, reps=3):
+    """Device time of torch_reference_handoff (CUDA events, after one warm-up
+    run), and how far its mapped rows are from the rows the fused kernels
+    installed in ``dst_pool`` before this call (relative Frobenius error and
+    max |difference|, both against BF16 outputs)."""
+    dev = src_pool.k_buffer.device
+    gpu_layers = [{k: (v.to(dev) if k != "selected" else v) for k, v in t.items()} for t in layers]
+    # The fused kernels' rows, read before the torch path overwrites them.
+    ours = torch.stack((dst_pool.k_buffer[:, dst_slots], dst_pool.v_buffer[:, dst_slots]))
+    mapped = torch_reference_handoff(gpu_layers, src_pool, src_slots, dst_pool, dst_slots, theta=theta)
+    err2 = ref2 = max_abs = 0.0
+    for kind in range(2):
+        for l in range(mapped.shape[1]):
+            m, o = mapped[kind, l].float(), ours[kind, l].float()
+            err2 += float((m - o).square().sum())
+            ref2 += float(m.square().sum())
+            max_abs = max(max_abs, float((m - o).abs().max()))
+    rel = math.sqrt(err2 / ref2)
+    del ours, mapped
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(reps):
+        torch_reference_handoff(gpu_layers, src_pool, src_slots, dst_pool, dst_slots, theta=theta)
+    b.record()
+    b.synchronize()
+    torch.cuda.empty_cache()
+    return a.elapsed_time(b) / reps, rel, max_abs
+
+
+# ----------------------------------------------------------------------------
 # CPU reference (oracle restatement of the reference's torch CPU path)
 # ----------------------------------------------------------------------------
 def cpu_reference_tokens_per_s(layers, *, n_sample, reps, seed=7):
@@ -413,6 +494,19 @@ def run_single(args):
     h2d = block_host.numel() * 2 + idx_host.numel() * 8
     del block_dev, block_host
 
+    # ---- the reference's torch path on this GPU (same pools and slot lists) ------
+    try:
+        ref_ms, ref_rel, ref_max = torch_reference_timing(layers, src_pool, src_slots, dst_pool, dst_slots,
+                                                          theta=theta)
+        ref_tps = n / (ref_ms / 1e3)
+        torch_ref = dict(ms=ref_ms, tokens_per_s=ref_tps, value_over_torch=value / ref_tps,
+                         rel_frobenius_vs_kernels=ref_rel, max_abs_vs_kernels=ref_max,
+                         path="pack_source_block (index_select per layer) + PageMapper.map_page (FP32, einsum "
+                              "per target layer) + per-layer set_kv_buffer, restated in torch on this GPU")
+    except Exception as exc:  # a failed baseline must not hide the bench line
+        torch_ref = dict(error=f"{type(exc).__name__}: {exc}"[:300])
+        torch.cuda.empty_cache()
+
     # ---- re-prefill estimate of the same history on this GPU ---------------------
     prefill = reprefill_estimate(dev, tokens=n, requests=1, tp=1)
     prefill["handoff_ms"] = statistics.median(step_ms)
@@ -453,6 +547,7 @@ def run_single(args):
         gpu_launches=launches_per_step * args.steps,
         clocks=clocks.summary(),
         reprefill_estimate=prefill,
+        torch_gpu_reference=torch_ref,
     )
     print(json.dumps(line), flush=True)
     return 0
