@@ -28,11 +28,12 @@
 //               group, warp w reads TMEM lane quarter w % 4 (token rows, one
 //               per thread), in four rounds of 16 RoPE pairs (columns i and
 //               i+64): target RoPE for keys (sin/cos of the exact FP32 phase
-//               after a Cody-Waite reduction by pi), BF16 packing, a swizzled
-//               32 x 64 B staging tile, then 16-byte stores of 8 rows x
-//               (2 x 32 B) per warp instruction; into this GPU's own pool
-//               with an L2 evict-first policy, so the stores do not push
-//               shared source rows out.
+//               after a Cody-Waite reduction by pi), BF16 packing into a
+//               swizzled 32 x 128 B staging tile that collects two rounds,
+//               then 16-byte stores of 4 rows x (2 x 64 B) per warp
+//               instruction, so two store instructions touch each row per
+//               m-tile; into this GPU's own pool with an L2 evict-first
+//               policy, so the stores do not push shared source rows out.
 //   warp 16     TMEM owner + single-thread tcgen05.mma issuer: per m-tile one
 //               K=16 step that loads the bias (a constant ones column times a
 //               [bias_hi, bias_lo] block), then 8 K=16 steps per 128-feature
@@ -432,9 +433,9 @@ __device__ __forceinline__ int cursor_token_raw(const MapTcParams& p, const Tile
 // eq*32 + lane (one per thread), accumulator n % 4. The destination slot of
 // the next m-tile is loaded while this one is processed.
 __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_base, int g, int eq, int lane) {
-  uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 64 B, this warp only
-  uint8_t* my_row = stage + lane * 64;
-  const int my_key = (lane >> 1) & 3;  // staging swizzle of this lane's row
+  uint8_t* stage = s.e_gen + (g * 4 + eq) * kEpiWarpBytes;  // 32 rows x 128 B, this warp only
+  uint8_t* my_row = stage + lane * 128;
+  const int my_key = lane & 7;  // staging swizzle of this lane's row
   const int64_t dst_stride_bytes = p.dst_row_stride * 2;
   const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(eq * 32) << 16);
   const int row_in_tile = eq * 32 + lane;
@@ -522,29 +523,37 @@ __device__ void run_epilogue(const MapTcParams& p, const Smem& s, uint32_t tmem_
           }
         }
       }
-      // Local chunk lc of the round's 64-byte row piece (0-1: columns
-      // [p0, p0+16), 2-3: [64+p0, ...)) sits at lc ^ ((row >> 1) & 3).
-      *reinterpret_cast<uint4*>(my_row + ((0 ^ my_key) << 4)) = pack8(ylo);
-      *reinterpret_cast<uint4*>(my_row + ((1 ^ my_key) << 4)) = pack8(ylo + 8);
-      *reinterpret_cast<uint4*>(my_row + ((2 ^ my_key) << 4)) = pack8(yhi);
-      *reinterpret_cast<uint4*>(my_row + ((3 ^ my_key) << 4)) = pack8(yhi + 8);
-      __syncwarp();
-      // Stores: 8 rows x (2 x 32 contiguous bytes) per warp instruction.
-      const int lc = lane & 3;
-      const int gchunk = lc < 2 ? 2 * r + lc : 8 + 2 * r + (lc - 2);
-#pragma unroll
-      for (int qq = 0; qq < 4; ++qq) {
-        const int rr = 8 * qq + (lane >> 2);
-        char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
-        const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 64 + ((lc ^ ((rr >> 1) & 3)) << 4));
-        if (dst != nullptr) {
-          if (p.dst_evict_first)
-            st_global_v4_hint(dst + gchunk * 16, v, store_policy);
-          else
-            *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
-        }
+      // Staging row (128 B): chunks 0-3 hold columns [32h, 32h+32) and chunks
+      // 4-7 columns [64+32h, ...) of the round pair h = r / 2; round r fills
+      // chunks 2(r&1), 2(r&1)+1 and 4+2(r&1), 4+2(r&1)+1. Chunk c sits at
+      // c ^ (row & 7).
+      {
+        const int c0 = 2 * (r & 1);
+        *reinterpret_cast<uint4*>(my_row + (((c0 + 0) ^ my_key) << 4)) = pack8(ylo);
+        *reinterpret_cast<uint4*>(my_row + (((c0 + 1) ^ my_key) << 4)) = pack8(ylo + 8);
+        *reinterpret_cast<uint4*>(my_row + (((c0 + 4) ^ my_key) << 4)) = pack8(yhi);
+        *reinterpret_cast<uint4*>(my_row + (((c0 + 5) ^ my_key) << 4)) = pack8(yhi + 8);
       }
-      __syncwarp();
+      if (r & 1) {
+        __syncwarp();
+        // Stores: 4 rows x (2 x 64 contiguous bytes) per warp instruction.
+        const int lc = lane & 7;
+        const int half = r >> 1;
+        const int gchunk = lc < 4 ? 4 * half + lc : 8 + 4 * half + (lc - 4);
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq) {
+          const int rr = 4 * qq + (lane >> 3);
+          char* dst = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(row_ptr), rr));
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((lc ^ (rr & 7)) << 4));
+          if (dst != nullptr) {
+            if (p.dst_evict_first)
+              st_global_v4_hint(dst + gchunk * 16, v, store_policy);
+            else
+              *reinterpret_cast<uint4*>(dst + gchunk * 16) = v;
+          }
+        }
+        __syncwarp();
+      }
     }
     cur = nxt;
     nxt = after;

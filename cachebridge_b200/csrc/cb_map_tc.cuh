@@ -21,7 +21,7 @@ constexpr int kLoaderWarp = kMmaWarp + 1;
 constexpr int kTcThreads = 32 * (kLoaderWarp + 1);
 constexpr int kAccBufs = 4;                    // FP32 accumulators in TMEM (128 columns each)
 constexpr int kTmemCols = 128 * kAccBufs;      // all 512 TMEM columns
-constexpr int kEpiWarpBytes = 32 * 64;         // 32 token rows x 64 B staging per epilogue warp
+constexpr int kEpiWarpBytes = 32 * 128;        // 32 token rows x 128 B staging per epilogue warp
 constexpr int kTcMaxSmem = 232448;             // sm_100 opt-in dynamic shared memory per block
 
 struct MapTcParams {
