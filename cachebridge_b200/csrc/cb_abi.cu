@@ -19,6 +19,7 @@
 #include "../../include/cachebridge_b200.h"
 #include "cb_kernels.cuh"
 #include "cb_map_tc.cuh"
+#include "cb_map_tm.cuh"
 
 namespace {
 
@@ -149,7 +150,22 @@ int check_rows(const cb_rows* r, const char* name, int head_dim, int heads_used,
   return CB_OK;
 }
 
-std::once_flag g_tc_attr_once[64];
+// cudaFuncSetAttribute result for the tensor-core kernels' shared-memory
+// opt-in, per device: set once, and its result (success or the error) is
+// returned to every later call on that device.
+struct AttrOnce {
+  std::once_flag once;
+  cudaError_t result = cudaSuccess;
+};
+AttrOnce g_tc_attr[64];
+AttrOnce g_tm_attr[64];
+
+cudaError_t set_smem_attr_once(AttrOnce& a, const void* kernel) {
+  std::call_once(a.once, [&] {
+    a.result = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cbk::kTcMaxSmem);
+  });
+  return a.result;
+}
 
 int check_rope(const cb_rope* r, int head_dim, const char* name) {
   if (r == nullptr) return fail(CB_ERR_INVALID, std::string(name) + ": null RoPE descriptor");
@@ -211,6 +227,9 @@ struct cb_mapper {
   int* sel_local = nullptr;
   int* used_dev = nullptr;
   uint8_t* w_img = nullptr;  // head_dim 128 only: [2][L_t][H][S][32 KB]
+  // head_dim 128 and KB <= 4 only: per unit KB * 16 chunks x 128 lanes x 16 B,
+  // the tensor-memory weight image of map_install_tm_kernel.
+  uint8_t* w_tm = nullptr;
 };
 
 namespace {
@@ -256,6 +275,14 @@ int launch_derotate(const cb_mapper* m, cudaStream_t st, const cb_rows* src, int
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "derotate_pack launch");
   return CB_OK;
+}
+
+// True when a target-RoPE phase of the call can reach 4e5 rad, beyond the
+// reduced-range trigonometry of the tensor-core epilogues.
+bool needs_exact_trig(const cb_rope* dst_rope, int64_t position_start, int64_t n_tokens) {
+  float max_inv = 0.f;
+  for (int i = 0; i < dst_rope->half_dim; ++i) max_inv = std::max(max_inv, std::fabs(dst_rope->inv_freq[i]));
+  return static_cast<double>(position_start + n_tokens) * max_inv > 4.0e5;
 }
 
 // M-tiles per work item of the tensor-core kernel. An item is one (target
@@ -345,24 +372,111 @@ int launch_tc(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.dst_magnitude = dst_rope->magnitude;
   p.position_start = position_start;
   p.order = order;
-  {
-    float max_inv = 0.f;
-    for (int i = 0; i < dst_rope->half_dim; ++i) max_inv = std::max(max_inv, std::fabs(dst_rope->inv_freq[i]));
-    p.trig_exact = static_cast<double>(position_start + n_tokens) * max_inv > 4.0e5 ? 1 : 0;
-  }
+  p.trig_exact = needs_exact_trig(dst_rope, position_start, n_tokens) ? 1 : 0;
   p.status = dev_status;
   const int smem = cbk::tc_smem_bytes(p.w_slots, p.stages);
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(g_tc_attr_once[m->device & 63], [&] {
-    attr_err = cudaFuncSetAttribute(cbk::map_install_tc_kernel,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, cbk::kTcMaxSmem);
-  });
+  const cudaError_t attr_err =
+      set_smem_attr_once(g_tc_attr[m->device & 63], reinterpret_cast<const void*>(cbk::map_install_tc_kernel));
   if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
   const int grid = static_cast<int>(std::min<int64_t>(items, m->num_sms));
   cbk::map_install_tc_kernel<<<grid, cbk::kTcThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "map_install_tc launch");
   return CB_OK;
+}
+
+// map_install_tm_kernel (weights in tensor memory) serves mappers of at most
+// four 128-feature blocks per unit, tokens in call order and phases inside the
+// reduced trigonometry range; map_install_tc_kernel takes every other call.
+bool tm_eligible(const cb_mapper* m, const cb_rope* dst_rope, int64_t position_start, int64_t n_tokens,
+                 const int32_t* order) {
+  return m->w_tm != nullptr && m->KB <= cbk::kTmMaxKB && order == nullptr &&
+         !needs_exact_trig(dst_rope, position_start, n_tokens);
+}
+
+int launch_tm(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst, int64_t n_tokens,
+              int64_t position_start, const cb_rope* dst_rope, const void* workspace, int32_t* dev_status) {
+  cbk::MapTmParams p{};
+  p.n_tokens = static_cast<int>(n_tokens);
+  p.L_t = m->L_t;
+  p.H = m->H;
+  p.S = m->S;
+  p.KB = m->KB;
+  p.kb_heads = m->Hs > 0 ? m->Hs : 1;
+  p.dense = m->Hs > 0 ? 1 : 0;
+  p.R = tc_chunk_mtiles(n_tokens, 2ll * m->H * m->L_t, m->num_sms);
+  p.n_chunks = static_cast<int>((n_tokens + p.R * cbk::kBM - 1) / (p.R * cbk::kBM));
+  const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
+  if (items > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "work too large for one call");
+  p.num_items = static_cast<int>(items);
+  p.stages = std::min(8, (cbk::kTcMaxSmem - cbk::tm_smem_bytes(0)) / cbk::kKBlockBytes);
+  if (p.stages < 2) return fail(CB_ERR_UNSUPPORTED, "shared memory too small for the pipeline");
+  // Two weight buffers when both fit beside the accumulators (S <= 2).
+  p.w_bufs = (512 - cbk::kTmWeightCol0) / (64 * m->KB) >= 2 ? 2 : 1;
+  p.w_tm = m->w_tm;
+  p.unit_bytes = static_cast<int64_t>(m->KB) * cbk::kKBlockBytes;
+  p.bias = m->b32;
+  p.sel_global = m->sel;
+  p.sel_local = m->sel_local;
+  for (int l = 0; l < src->layers; ++l) p.src_v[l] = src->v[l];
+  p.src_row_stride = src->row_stride;
+  p.src_rows = src->rows;
+  p.src_head_offset = src->head_offset;
+  p.src_slot_dtype = src->slot_dtype;
+  p.src_slots = src->slots;
+  {
+    const cuuint64_t kdims[4] = {128, static_cast<cuuint64_t>(ws_heads(m)), static_cast<cuuint64_t>(n_tokens),
+                                 static_cast<cuuint64_t>(m->U)};
+    const cuuint64_t kstr[3] = {256, static_cast<cuuint64_t>(ws_heads(m)) * 256,
+                                static_cast<cuuint64_t>(n_tokens) * ws_heads(m) * 256};
+    const cuuint32_t kbox[4] = {64, 1, 128, 1};
+    int rc = encode_bf16_map(&p.kmap, 4, workspace, kdims, kstr, kbox);
+    if (rc != CB_OK) return rc;
+  }
+  for (int l = 0; l < dst->layers; ++l) {
+    p.dst_k[l] = dst->k[l];
+    p.dst_v[l] = dst->v[l];
+  }
+  p.dst_row_stride = dst->row_stride;
+  p.dst_rows = dst->rows;
+  p.dst_head_offset = dst->head_offset;
+  p.dst_slot_dtype = dst->slot_dtype;
+  p.dst_slots = dst->slots;
+  p.dst_evict_first = rows_on_device(m->device, dst) ? 1 : 0;
+  p.dst_v8 = (dst->row_stride * 2) % 32 == 0 ? 1 : 0;
+  for (int l = 0; l < dst->layers && p.dst_v8; ++l)
+    if (reinterpret_cast<uintptr_t>(dst->k[l]) % 32 || reinterpret_cast<uintptr_t>(dst->v[l]) % 32) p.dst_v8 = 0;
+  for (int i = 0; i < 64; ++i) {
+    const float inv = dst_rope->inv_freq[i];
+    p.dst_inv_freq[i] = inv;
+    // Unit rotations by one and by eight positions of the exact angle.
+    p.rot1_c[i] = static_cast<float>(std::cos(static_cast<double>(inv)));
+    p.rot1_s[i] = static_cast<float>(std::sin(static_cast<double>(inv)));
+    p.rot8_c[i] = static_cast<float>(std::cos(8.0 * static_cast<double>(inv)));
+    p.rot8_s[i] = static_cast<float>(std::sin(8.0 * static_cast<double>(inv)));
+  }
+  p.dst_magnitude = dst_rope->magnitude;
+  p.position_start = position_start;
+  p.order = nullptr;
+  p.status = dev_status;
+  const cudaError_t attr_err =
+      set_smem_attr_once(g_tm_attr[m->device & 63], reinterpret_cast<const void*>(cbk::map_install_tm_kernel));
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err, "cudaFuncSetAttribute");
+  const int grid = static_cast<int>(std::min<int64_t>(items, m->num_sms));
+  cbk::map_install_tm_kernel<<<grid, cbk::kTmThreads, cbk::tm_smem_bytes(p.stages), st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "map_install_tm launch");
+  return CB_OK;
+}
+
+// The tensor-core map + install phase: the transposed kernel where it
+// applies, else the general one.
+int launch_map(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_rows* dst, int64_t n_tokens,
+               int64_t position_start, const cb_rope* dst_rope, const void* workspace, const int32_t* order,
+               int32_t* dev_status) {
+  if (tm_eligible(m, dst_rope, position_start, n_tokens, order))
+    return launch_tm(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, dev_status);
+  return launch_tc(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, order, dev_status);
 }
 
 int check_tc_extras(const cb_mapper* m, int dtype, int64_t n_tokens, const void* workspace,
@@ -585,6 +699,30 @@ int mapper_create(cb_mapper** out, int device, int target_layers, int heads, int
     }
     if ((e = cudaMalloc(&m->w_img, img.size() * sizeof(uint16_t))) != cudaSuccess) return cleanup(e, "cudaMalloc w_img");
     if ((e = cudaMemcpy(m->w_img, img.data(), img.size() * sizeof(uint16_t), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload w_img");
+    if (m->KB <= cbk::kTmMaxKB) {
+      // Tensor-memory image: per unit, chunk c (input features 8c..8c+7) of
+      // lane L (output feature tm_lane_feature(L)) at (c * 128 + L) * 16 B.
+      const size_t unit_halfs_tm = static_cast<size_t>(m->KB) * cbk::kKBlockBytes / 2;
+      std::vector<uint16_t> tm(units * unit_halfs_tm, 0);
+      for (int kind = 0; kind < 2; ++kind) {
+        const float* W = kind ? v_weight : k_weight;
+        for (int l = 0; l < target_layers; ++l)
+          for (int h = 0; h < heads; ++h) {
+            const float* wh = W + (static_cast<size_t>(l) * heads + h) * F * head_dim;
+            const size_t unit = (static_cast<size_t>(kind) * target_layers + l) * heads + h;
+            uint16_t* base = tm.data() + unit * unit_halfs_tm;
+            for (int c = 0; c < F / 8; ++c)
+              for (int L = 0; L < 128; ++L) {
+                const int f = cbk::tm_lane_feature(L);
+                for (int e8 = 0; e8 < 8; ++e8)
+                  base[(static_cast<size_t>(c) * 128 + L) * 8 + e8] =
+                      f32_to_bf16_rne(wh[static_cast<size_t>(8 * c + e8) * head_dim + f]);
+              }
+          }
+      }
+      if ((e = cudaMalloc(&m->w_tm, tm.size() * sizeof(uint16_t))) != cudaSuccess) return cleanup(e, "cudaMalloc w_tm");
+      if ((e = cudaMemcpy(m->w_tm, tm.data(), tm.size() * sizeof(uint16_t), cudaMemcpyHostToDevice)) != cudaSuccess) return cleanup(e, "upload w_tm");
+    }
   }
   *out = m;
   return CB_OK;
@@ -603,6 +741,7 @@ int cb_mapper_destroy(cb_mapper* m) {
   cudaFree(m->sel_local);
   cudaFree(m->used_dev);
   cudaFree(m->w_img);
+  cudaFree(m->w_tm);
   delete m;
   return CB_OK;
 }
@@ -666,7 +805,7 @@ int cb_map_install(cb_mapper* m, void* stream, const cb_rows* src, const cb_rows
     if ((rc = launch_derotate(m, st, src, n_tokens, position_start, src_rope, workspace, token_order,
                               dev_status)) != CB_OK)
       return rc;
-    return launch_tc(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, token_order, dev_status);
+    return launch_map(m, st, src, dst, n_tokens, position_start, dst_rope, workspace, token_order, dev_status);
   }
 
   // Generic CUDA-core path.
@@ -741,7 +880,7 @@ int cb_map_install_packed(cb_mapper* m, void* stream, const cb_rows* src, const 
   if (!guard.ok) return fail(CB_ERR_CUDA, "cudaSetDevice failed");
   if ((rc = ensure_rows_access(m->device, src, "src rows")) != CB_OK) return rc;
   if ((rc = ensure_rows_access(m->device, dst, "dst rows")) != CB_OK) return rc;
-  return launch_tc(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, position_start, dst_rope, workspace,
+  return launch_map(m, static_cast<cudaStream_t>(stream), src, dst, n_tokens, position_start, dst_rope, workspace,
                    token_order,
                    dev_status);
 }

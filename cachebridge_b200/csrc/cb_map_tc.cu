@@ -44,10 +44,9 @@
 //               per m-tile otherwise.
 // Every wait is bounded (kWaitTimeoutNs): an expired wait flags
 // CB_DEV_ERR_TIMEOUT and the CTA unwinds instead of hanging.
-#include <climits>
-
 #include "cb_device.cuh"
 #include "cb_map_tc.cuh"
+#include "cb_pipeline.cuh"
 
 namespace cbk {
 
@@ -63,30 +62,6 @@ constexpr int kBarBFull = 24;     // [1]  loader -> MMA (bias block filled)
 constexpr int kBarBEmpty = 25;    // [1]  MMA -> loader (bias block consumed)
 constexpr int kBarDone = 26;      // [1]  MMA drain at exit
 constexpr int kNumBars = 32;
-
-struct Item {
-  int kind;   // 0 = K, 1 = V
-  int h;      // head within this call
-  int l;      // target layer
-  int tok0;   // first token of the chunk
-  int mtiles; // valid 128-token m-tiles in the chunk
-};
-
-__device__ __forceinline__ Item decode_item(const MapTcParams& p, int i) {
-  Item it;
-  const int per_hk = p.n_chunks * p.L_t;
-  const int hk = i / per_hk;
-  const int rem = i - hk * per_hk;
-  const int c = rem / p.L_t;
-  it.l = rem - c * p.L_t;
-  it.h = hk >> 1;
-  it.kind = hk & 1;
-  it.tok0 = c * p.R * kBM;
-  const int remaining = p.n_tokens - it.tok0;
-  const int mt = (remaining + kBM - 1) / kBM;
-  it.mtiles = mt < p.R ? mt : p.R;
-  return it;
-}
 
 struct Smem {
   uint32_t w;      // weight slots (shared::cta address)
@@ -133,120 +108,6 @@ __device__ __forceinline__ void sincos_half_turns(float phi, float& c, float& s,
   r = fmaf(-kf, kP2, r);
   __sincosf(r, &s, &c);
   sign = static_cast<uint32_t>(static_cast<int>(kf)) << 31;
-}
-
-// Token lookups. A row's token is token_order[t] (or t) for processing index
-// t; the producers and the epilogue read the order entry two m-tiles ahead
-// and the slot one m-tile ahead, so neither dependent load stalls a pipeline
-// role. kNoToken marks a row past the call's (or item's) end.
-constexpr int kNoToken = INT_MIN;
-
-__device__ __forceinline__ int item_token_raw(const MapTcParams& p, const Item& it, int mm, int row) {
-  if (mm >= it.mtiles) return kNoToken;
-  const int t = it.tok0 + mm * kBM + row;
-  if (t >= p.n_tokens) return kNoToken;
-  return p.order == nullptr ? t : __ldg(p.order + t);
-}
-
-// A token read by item_token_raw, or -1 for none. An order entry outside
-// [0, n) flags CB_DEV_ERR_SLOT_RANGE and the row is skipped.
-__device__ __forceinline__ int check_token(const MapTcParams& p, int raw) {
-  if (raw == kNoToken) return -1;
-  if (raw < 0 || raw >= p.n_tokens) {
-    flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-    return -1;
-  }
-  return raw;
-}
-
-// ------------------------------- producers ---------------------------------
-// Four warps; warp pw owns token rows [32 pw, 32 pw + 32) of every stage.
-// Keys: thread 0 loads the stage with two 4-D TMA boxes (128 tokens x 64
-// features) from the content-space workspace (expect_tx 32 KB). Values:
-// 16-byte cp.async gathers of the source pool rows through the slot table,
-// 16 lanes per 256-byte row, two rows per warp instruction, tracked by
-// cp.async.mbarrier.arrive.noinc. The stage's full barrier counts 129
-// arrivals: one per producer thread plus thread 0's expect_tx.
-__device__ void run_producer(const MapTcParams& p, const Smem& s, int pw, int lane) {
-  const int NS = p.stages;
-  const bool leader = pw == 0 && lane == 0;
-  int stage = 0;
-  uint32_t phase = 0;
-  bool ok = true;
-  for (int i = blockIdx.x; i < p.num_items && ok; i += gridDim.x) {
-    const Item it = decode_item(p, i);
-    // Source slot of this lane's row (values only): tok_c / row_c for m-tile
-    // m, raw_n the order entry of m-tile m + 1.
-    const int row_in_tile = pw * 32 + lane;
-    int tok_c = -1, raw_n = kNoToken;
-    int64_t row_c = 0;
-    if (it.kind == 1) {
-      tok_c = check_token(p, item_token_raw(p, it, 0, row_in_tile));
-      if (tok_c >= 0) row_c = load_slot(p.src_slots, p.src_slot_dtype, tok_c);
-      raw_n = item_token_raw(p, it, 1, row_in_tile);
-    }
-    for (int m = 0; m < it.mtiles && ok; ++m) {
-      const int tok0 = it.tok0 + m * kBM;
-      int valid = tok_c >= 0;
-      const int64_t srow = row_c;
-      if (it.kind == 1) {
-        tok_c = check_token(p, raw_n);
-        row_c = tok_c >= 0 ? load_slot(p.src_slots, p.src_slot_dtype, tok_c) : 0;
-        raw_n = item_token_raw(p, it, m + 2, row_in_tile);
-      }
-      if (it.kind == 1 && valid && (srow < 0 || srow >= p.src_rows)) {
-        flag_error(p.status, CB_DEV_ERR_SLOT_RANGE);
-        valid = 0;
-      }
-      for (int kb = 0; kb < p.KB; ++kb) {
-        // Feature block kb: selected layer j, source head sh (the target head
-        // itself for headwise maps, every source head in turn for dense ones).
-        const int j = kb / p.kb_heads;
-        const int sh = p.dense ? kb - j * p.kb_heads : it.h;
-        // Warp-uniform outcome: the gather below uses full-warp shuffles.
-        const bool got = mbar_wait(bar_at(s, kBarEmpty + stage), phase ^ 1u, s.abort_flag, p.status);
-        if (!__all_sync(0xffffffffu, got)) {
-          ok = false;
-          break;
-        }
-        const uint32_t full = bar_at(s, kBarFull + stage);
-        const uint32_t dst = s.a + stage * kKBlockBytes;
-        if (it.kind == 0) {
-          if (leader) {
-            const int u = __ldg(p.sel_local + it.l * p.S + j);
-            mbar_arrive_expect_tx(full, kKBlockBytes);
-            tma_load_4d(dst, &p.kmap, 0, sh, tok0, u, full);
-            tma_load_4d(dst + kPanelBytes, &p.kmap, 64, sh, tok0, u, full);
-          }
-          mbar_arrive(full);
-        } else {
-          const int sl = __ldg(p.sel_global + it.l * p.S + j);
-          const char* base = reinterpret_cast<const char*>(p.src_v[sl]) +
-                             static_cast<int64_t>(p.src_head_offset + sh) * (kD * 2);
-          const int64_t stride_bytes = p.src_row_stride * 2;
-          const int c = lane & 15;
-#pragma unroll
-          for (int ii = 0; ii < 16; ++ii) {
-            const int r = 2 * ii + (lane >> 4);
-            const int64_t rr = __shfl_sync(0xffffffffu, srow, r);
-            const int vv = __shfl_sync(0xffffffffu, valid, r);
-            const int row = pw * 32 + r;
-            const char* g = base + (vv ? rr * stride_bytes : 0) + c * 16;
-            const uint32_t d = dst + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-            cp_async_16(d, g, vv ? 16u : 0u);
-          }
-          cp_async_arrive_noinc(full);
-          if (leader) mbar_arrive(full);
-        }
-        if (++stage == NS) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-  }
-  // Never exit with copies in flight into shared memory.
-  cp_async_wait_all();
 }
 
 // ------------------------------ weight loader ------------------------------
@@ -623,7 +484,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
   const uint32_t tmem_base = *s.tmem_holder;
 
   if (warp < kProdWarps) {
-    run_producer(p, s, warp, lane);
+    run_producer(p, StageRing{s.a, s.bars, kBarFull, kBarEmpty}, s.abort_flag, warp, lane);
   } else if (warp < kMmaWarp) {
     // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule).
     run_epilogue(p, s, tmem_base, (warp - kProdWarps) >> 2, warp & 3, lane);
