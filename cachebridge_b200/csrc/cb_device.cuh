@@ -57,6 +57,14 @@ __device__ __forceinline__ void flag_error(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(reinterpret_cast<int*>(status), bits);
 }
 
+// True once a bounded wait on this device has expired (CB_DEV_ERR_TIMEOUT is
+// set in the status word). The handoff kernels then do no work: a chunk whose
+// receive slot never filled is not mapped or installed, and the chunks after
+// it are skipped too, until the caller reads and clears the status word.
+__device__ __forceinline__ bool status_timed_out(const int32_t* status) {
+  return status != nullptr && (*reinterpret_cast<const volatile int32_t*>(status) & CB_DEV_ERR_TIMEOUT) != 0;
+}
+
 // Token handled at processing index i of a call: token_order[i] when the
 // caller gave an order (a permutation of [0, n)), else i. An entry outside
 // [0, n) flags CB_DEV_ERR_SLOT_RANGE and returns -1 (the row is skipped).

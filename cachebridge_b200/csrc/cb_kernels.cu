@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + warp;
-  if (t >= p.n_tokens) return;
+  if (t >= p.n_tokens || status_timed_out(p.status)) return;
   const int g = lane >> 3;
   const int j = lane & 7;
 
@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const __grid_constant__ 
   const int64_t groups_per_kl = (p.n + RPW - 1) / RPW;
   const int64_t groups_total = 2 * static_cast<int64_t>(p.layers) * groups_per_kl;
   const int lane = threadIdx.x & 31;
+  if (status_timed_out(p.status)) return;
   const int nvec = p.row_bytes / static_cast<int>(sizeof(V));
   for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
        w < groups_total; w += warps_total) {
@@ -220,6 +221,10 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { retu
 template <typename T>
 __global__ void __launch_bounds__(256) map_install_simt_kernel(const __grid_constant__ SimtParams p) {
   extern __shared__ float sm_f[];
+  __shared__ int skip;
+  if (threadIdx.x == 0) skip = status_timed_out(p.status) ? 1 : 0;
+  __syncthreads();
+  if (skip) return;
   const int64_t t = blockIdx.x;
   const int l = blockIdx.y;
   const int kind = blockIdx.z;

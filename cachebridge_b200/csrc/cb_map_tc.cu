@@ -461,7 +461,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
     mbar_init(bar_at(s, kBarBFull), 1);
     mbar_init(bar_at(s, kBarBEmpty), 1);
     mbar_init(bar_at(s, kBarDone), 1);
-    *s.abort_flag = 0;
+    // A device timeout before this launch: every role skips its work.
+    *s.abort_flag = status_timed_out(p.status) ? 1 : 0;
     fence_mbarrier_init();
   }
   // Constant operands: the ones block (rows of [1, 1, 0 x 14], no-swizzle
@@ -483,7 +484,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) map_install_tc_kernel(const __g
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_holder;
 
-  if (warp < kProdWarps) {
+  if (*s.abort_flag) {
+    // Skipped launch (see status_timed_out).
+  } else if (warp < kProdWarps) {
     run_producer(p, StageRing{s.a, s.bars, kBarFull, kBarEmpty}, s.abort_flag, warp, lane);
   } else if (warp < kMmaWarp) {
     // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule).

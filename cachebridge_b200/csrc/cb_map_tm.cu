@@ -499,7 +499,8 @@ __global__ void __launch_bounds__(kTmThreads, 1) map_install_tm_kernel(const __g
       mbar_init(bar_at(s, kBarStaged + g), 4);
       mbar_init(bar_at(s, kBarFree + g), 4);
     }
-    *s.abort_flag = 0;
+    // A device timeout before this launch: every role skips its work.
+    *s.abort_flag = status_timed_out(p.status) ? 1 : 0;
     fence_mbarrier_init();
   }
   if (warp == kTmMmaWarp) {
@@ -511,7 +512,9 @@ __global__ void __launch_bounds__(kTmThreads, 1) map_install_tm_kernel(const __g
   tc_fence_after();
   const uint32_t tmem_base = *s.tmem_holder;
 
-  if (warp < kTmProdWarps) {
+  if (*s.abort_flag) {
+    // Skipped launch (see status_timed_out).
+  } else if (warp < kTmProdWarps) {
     run_producer(p, StageRing{s.a, s.bars, kBarFull, kBarEmpty}, s.abort_flag, warp, lane);
   } else if (warp < kTmMmaWarp) {
     // TMEM lane quarter = warp % 4 (tcgen05.ld lane-access rule).

@@ -56,7 +56,15 @@ extern "C" {
 #define CB_ERR_CUDA -3        /* a CUDA runtime call failed */
 #define CB_ERR_ALIAS -4       /* destination rows alias (install) */
 
-/* Device status bits, OR-ed into the caller's int32 status word. */
+/*
+ * Device status bits, OR-ed into the caller's int32 status word. Once
+ * CB_DEV_ERR_TIMEOUT is set in a status word, the map, pack and install
+ * kernels given that word do nothing (a chunk whose receive slot never filled
+ * is neither mapped nor installed, and the chunks queued after it are skipped)
+ * until the caller reads and clears the word. Rows those kernels would have
+ * written keep whatever they held; after a failed publication vote they are
+ * undefined until the caller frees or rewrites them.
+ */
 #define CB_DEV_ERR_SLOT_RANGE 1 /* a source or destination slot was outside [0, rows) */
 #define CB_DEV_ERR_TIMEOUT 2    /* a bounded pipeline wait inside a kernel expired */
 
@@ -215,8 +223,12 @@ CB_API int cb_map_install(cb_mapper* mapper, void* stream, const cb_rows* src,
  * before any stream capture. Every call on a device shares the one array:
  * calls whose GPU work can overlap (streams not ordered with one another,
  * concurrent host threads) race on it and must be serialised by the caller.
- * Nothing in the array needs to start at zero. Arguments and results are
- * those of cb_map_install with token_order NULL.
+ * Nothing in the array needs to start at zero. The array is part of the
+ * library's device code: every device on which that code is loaded (with
+ * CUDA's eager module loading, every device the process uses with this
+ * library loaded) holds the 64 MiB until the process exits, whether or not
+ * this entry point is ever called. Arguments and results are those of
+ * cb_map_install with token_order NULL.
  */
 #define CB_NOALLOC_SCRATCH_BYTES (64 << 20)
 CB_API int cb_map_install_noalloc(cb_mapper* mapper, void* stream, const cb_rows* src,

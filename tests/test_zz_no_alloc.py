@@ -2,11 +2,11 @@
 from the library's fixed per-device array instead of from the caller.
 
 Checked through the C ABI against cb_map_install (caller workspace) on the
-same inputs, for two calls in a row that share the array. Tolerance: the BF16
-bound of the tensor-core path (the GPU parity tests' own),
-    relative Frobenius error          <= 5e-3
-    max |ours - theirs| / max(1, |theirs|) <= 2e-2,
-with untouched rows compared bit for bit. The file sorts last so that it runs
+same inputs, for two calls in a row that share the array. Both calls run the
+same deterministic kernels on the same inputs, so the written rows must be
+bit-identical (a scratch-sharing fault that perturbs a few values, such as a
+stale key row of the first request read during the second, fails this), and
+untouched rows must keep their canary. The file sorts last so that it runs
 after every other test, and it also runs alone in a fresh process (where its
 first call performs the per-device set-up).
 """
@@ -39,14 +39,6 @@ def _mapper_dir(tmp_path, seed):
             t[f"{kind}_bias"] = (torch.randn(H, D, generator=g) * 0.1).bfloat16().float()
         save_file(t, str(tmp_path / f"layer_{l:03d}.safetensors"))
     return tmp_path
-
-
-def _close(ours: torch.Tensor, theirs: torch.Tensor) -> None:
-    ours, theirs = ours.float().cpu(), theirs.float().cpu()
-    rf = float((ours - theirs).norm() / theirs.norm().clamp_min(1e-30))
-    norm_err = float(((ours - theirs).abs() / theirs.abs().clamp_min(1.0)).max())
-    assert rf <= 5e-3, f"relative Frobenius {rf:.3e}"
-    assert norm_err <= 2e-2, f"normalised max error {norm_err:.3e}"
 
 
 def _noalloc(mapper, src: RowSet, dst: RowSet, n: int, position_start: int) -> int:
@@ -97,7 +89,7 @@ def test_noalloc_matches_caller_workspace_on_two_calls(tmp_path, cuda_device):
         loc = dst_slots.cpu()
         written[loc] = True
         for a, b in ((got.k_buffer, ref.k_buffer), (got.v_buffer, ref.v_buffer)):
-            _close(a[:, loc.to(cuda_device)], b[:, loc.to(cuda_device)])
+            assert torch.equal(a[:, loc.to(cuda_device)], b[:, loc.to(cuda_device)]), "written rows differ"
     for buf in (got.k_buffer, got.v_buffer):
         assert bool((buf[:, (~written).to(cuda_device)].float() == CANARY).all()), "an untouched row changed"
 
