@@ -3,7 +3,8 @@
 Drop-in for ``cachebridge.online.blocks`` (src/cachebridge/online/blocks.py,
 duplicated in backends/sglang/runtime/bounded_cachebridge_core.py):
 
-- ``SourceLease``           single in-flight block ownership (blocks.py:11-43)
+- ``SourceLease``           single in-flight block ownership (blocks.py:11-43), a
+                            one-buffer ``SlotLedger``
 - ``pack_source_block``     gather pool rows into one contiguous workspace
                             (blocks.py:47-82), one ``cb_pack_rows`` launch instead
                             of 2*layers ``index_select`` launches
@@ -12,7 +13,8 @@ duplicated in backends/sglang/runtime/bounded_cachebridge_core.py):
                             of map_page + per-layer ``set_kv_buffer``
 - ``map_install_block``     the fully fused source-pool -> target-pool path (no
                             packed block at all): gather, map and install
-- ``install_unpublished``   publish-after-vote transaction (blocks.py:114-171)
+- ``install_unpublished``   publish-after-vote transaction (blocks.py:114-171), run
+                            on a ``HandoffTransaction`` (online/transaction.py)
 """
 
 from __future__ import annotations
@@ -20,42 +22,41 @@ from __future__ import annotations
 import torch
 
 from ..device import RowSet, pack_rows
+from .transaction import HandoffTransaction, SlotLedger
 
 
-class SourceLease:
-    """Single in-flight block; release is legal only after consumer completion."""
+class SourceLease(SlotLedger):
+    """Single in-flight block; release is legal only after consumer completion.
+
+    The reference's one-buffer lease (online/blocks.py:11-43) as a
+    ``SlotLedger`` of one buffer: ``begin`` opens it (restarting at token 0),
+    ``export`` claims the buffer for the next ordered block, ``acknowledge``
+    settles it once the consumer's GPU reads completed, ``close`` releases.
+    The error messages are the reference's, which callers match on.
+    """
 
     def __init__(self, acquire, release):
-        self.acquire = acquire
-        self.release = release
-        self.active = False
-        self.pending = False
-        self.next_start = 0
+        super().__init__(1, acquire, release, restart_on_open=True, messages=dict(
+            open="source lease already active", order="block ownership/order violation",
+            settle="consumer GPU completion required before buffer reuse",
+            close="cannot release source lease with outstanding GPU reads"))
+
+    @property
+    def active(self) -> bool:
+        return self.is_open
+
+    @property
+    def pending(self) -> bool:
+        return self.held[0]
 
     def begin(self):
-        if self.active:
-            raise RuntimeError("source lease already active")
-        self.acquire()
-        self.active = True
-        self.next_start = 0
+        self.open()
 
     def export(self, start, stop):
-        ordered = self.active and not self.pending and start == self.next_start and stop > start
-        if not ordered:
-            raise RuntimeError("block ownership/order violation")
-        self.pending = True
-        self.next_start = stop
+        self.claim(0, start, stop)
 
     def acknowledge(self, *, gpu_reads_complete):
-        if not (self.active and self.pending and gpu_reads_complete):
-            raise RuntimeError("consumer GPU completion required before buffer reuse")
-        self.pending = False
-
-    def close(self):
-        if not self.active or self.pending:
-            raise RuntimeError("cannot release source lease with outstanding GPU reads")
-        self.release()
-        self.active = False
+        self.settle(0, gpu_reads_complete=gpu_reads_complete)
 
 
 @torch.inference_mode()
@@ -162,38 +163,35 @@ def install_unpublished(
 ):
     """Allocate, write ordered gap-free blocks, vote on all ranks, then publish.
 
-    ``blocks`` yields ``(start, stop, value)``. Every rank reaches
-    ``ready_vote`` even after a local failure; pages are freed exactly once on
-    a local failure or a failed vote, never published while any rank is still
-    writing, and kept (not freed) if the vote itself cannot complete, because a
-    broken group cannot certify that all GPU writes stopped.
+    The reference's single-round contract (online/blocks.py:114-171), run on a
+    ``HandoffTransaction``: ``blocks`` yields ``(start, stop, value)``; each
+    block is checked for order before ``write(value, indices, start)`` and
+    counted after ``synchronize()``; a cancellation point counts written
+    blocks. Every rank reaches ``ready_vote`` even after a local failure. On a
+    local failure or a failed vote the rows are freed exactly once and
+    ``RuntimeError("unpublished target transaction rolled back")`` is raised;
+    if ``synchronize`` or the vote itself raises, the exception propagates and
+    the rows stay owned (a broken group cannot certify that GPU writes
+    stopped). Returns ``{"tokens", "blocks", "published"}``.
     """
-    indices = None
-    error = None
-    written = 0
-    cursor = 0
-    try:
-        indices = allocate(token_count)
-        if indices is None:
-            raise RuntimeError("target pool allocation failed")
-        for start, stop, value in blocks:
-            if start != cursor or not start < stop <= token_count or value.shape[2] != stop - start:
-                raise ValueError("missing, duplicate or overlapping block")
-            write(value, indices, start)
-            synchronize()
-            cursor = stop
-            written += 1
-            if cancel_after_blocks == written:
-                raise RuntimeError("controlled cancellation before publication")
-        if cursor != token_count:
-            raise ValueError("incomplete prefix")
-    except Exception as exc:  # noqa: BLE001 - every local failure must still vote
-        error = exc
+    txn = HandoffTransaction("install_unpublished", token_count, allocate=allocate, free=free,
+                             cancel_after_chunks=cancel_after_blocks)
+    indices = txn.begin()
+    if txn.error is None:
+        try:
+            for start, stop, value in blocks:
+                if start != txn.cursor or not start < stop <= token_count or value.shape[2] != stop - start:
+                    raise ValueError("missing, duplicate or overlapping block")
+                write(value, indices, start)
+                synchronize()
+                if not txn.chunk(start, stop):
+                    break
+        except Exception as exc:  # noqa: BLE001 - every local failure must still vote
+            txn.fail(exc)
     synchronize()
-    all_ready = ready_vote(error is None)  # a broken group propagates: pages stay owned
-    if error is not None or not all_ready:
-        if indices is not None:
-            free(indices)
-        raise RuntimeError("unpublished target transaction rolled back") from error
+    all_ready = ready_vote(txn.ready)  # raises through: the rows stay owned
+    if not (txn.ready and all_ready):
+        txn._free_once()
+        raise RuntimeError("unpublished target transaction rolled back") from txn.error
     publish(indices)
-    return dict(tokens=cursor, blocks=written, published=True)
+    return dict(tokens=txn.cursor, blocks=txn.chunks, published=True)

@@ -12,10 +12,11 @@ buffer), replacing the reference's export -> ``cudaMemcpyPeerAsync`` span
 loop (backends/sglang/runtime/peer_adapter.py:211-282, peer_runtime.py:55-64)
 and its IPC export (bounded_handoff_channel.py:83-123).
 
-Publication follows install_unpublished (src/cachebridge/online/blocks.py:114-171)
-and the all-rank vote of source_mapper_adapter.py:543-548: every rank votes
-after its stream work, and the prefix is published only if all ranks are
-ready.
+Publication goes through ``online.transaction``: each request is a
+``HandoffTransaction`` (target rows allocated unpublished, chunks recorded in
+order), and ``commit`` waits for the rank's GPU work, votes on all ranks and
+publishes, rolls back or quarantines (src/cachebridge/online/blocks.py:114-171,
+source_mapper_adapter.py:543-548 and :1145-1237).
 """
 
 from __future__ import annotations
@@ -27,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 from ..device import RawRows, RowSet, status_word
+from .transaction import SlotLedger
 
 
 @dataclass(frozen=True)
@@ -274,7 +276,13 @@ class TargetPlacement:
     Every rank of the pair builds one with the same ``requests`` (lists of
     ``(source_slots, target_slots)`` device tensors) and ``chunk``; the source
     passes ``source_pool``, the target ``mapper`` and ``target_pool``. The
-    constructor is collective over ``group`` (all ranks of the world).
+    constructor is collective over ``group`` (all ranks of the world). On the
+    target, the prepared calls read each request's target rows from a buffer
+    of their own: ``set_target_rows`` replaces them (for rows allocated per
+    handoff), ``target_slots`` starts them. Host-side ownership of the receive
+    slots is kept in a ``SlotLedger``: a chunk claims its slot, and the slot
+    is settled when the next chunk that uses it is queued behind the device
+    wait for its consumption.
     """
 
     def __init__(self, plan: PairPlan, requests, *, chunk: int, source_layers: int, device: torch.device,
@@ -318,6 +326,9 @@ class TargetPlacement:
         else:
             payload = dict(consumed=_export(flags), uuid=uuid, slots=self.SLOTS, chunk=chunk)
         self.flags = flags
+        self.ledger = SlotLedger(self.SLOTS, restart_on_open=True)
+        self.request_tokens = [len(s) for s, _ in requests]
+        self.bytes_per_token = 2 * source_layers * H * D * elem
         torch.cuda.synchronize(self.device)
         gathered = [None] * plan.world
         dist.all_gather_object(gathered, payload, group=group)
@@ -356,12 +367,15 @@ class TargetPlacement:
             # One key workspace, sized for the largest chunk, shared in stream order.
             biggest = max((b - a for _, a, b in self.chunks), default=0)
             ws = torch.empty(max(mapper.workspace_bytes(dtype, biggest), 16), dtype=torch.uint8, device=self.device)
+            self.workspace_bytes = ws.numel() + self.SLOTS * self.slot_bytes
+            # Each request's target rows, read by its prepared calls.
+            self.target_rows = [t.to(self.device, torch.int64).clone() for _, t in requests]
             self.calls = []
             for i, (q, a, b) in enumerate(self.chunks):
                 n = b - a
                 page = self.recv[i % self.SLOTS, : 2 * source_layers * n * H * D].view(2, source_layers, n, H, D)
-                self.calls.append(mapper.prepare(RowSet.from_page(page), target_pool.rows(requests[q][1][a:b]), n, a,
-                                                 workspace=ws))
+                self.calls.append(mapper.prepare(RowSet.from_page(page), target_pool.rows(self.target_rows[q][a:b]), n,
+                                                 a, workspace=ws))
 
     @property
     def launches(self) -> int:
@@ -373,15 +387,40 @@ class TargetPlacement:
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
-    def run(self) -> None:
-        """Enqueue every chunk of every request on the current stream."""
+    def set_target_rows(self, request: int, rows: torch.Tensor) -> None:
+        """Target rank: install request ``request`` into ``rows`` (a device
+        index tensor of the request's length) from the next ``run`` on; the
+        copy is queued on the current stream."""
+        if self.plan.role != "target":
+            raise RuntimeError("only the target rank owns target rows")
+        if rows is None or rows.numel() != self.target_rows[request].numel():
+            raise ValueError("target rows must match the request's token count")
+        self.target_rows[request].copy_(rows, non_blocking=True)
+
+    def run(self, transactions=None) -> None:
+        """Enqueue every chunk of every request on the current stream.
+
+        ``transactions`` (one ``HandoffTransaction`` per request, optional)
+        receive each chunk as it is queued, with its logical bytes: raw source
+        rows on either rank. The device pipeline queues every chunk even after
+        a transaction failed, so both ranks' device handshakes stay paired;
+        the failed transaction is rolled back at commit.
+        """
         from .. import _native as nat
 
         st = self._stream()
         status = self.status.data_ptr()
+        self.ledger.open()
         for i in range(len(self.chunks)):
             c = self.counter
             slot = i % self.SLOTS  # fixed per chunk: the target's prepared calls read it
+            if self.ledger.held[slot]:
+                # Its previous chunk's consumption is awaited on the device before reuse.
+                self.ledger.settle(slot, gpu_reads_complete=True)
+            q, a, b = self.chunks[i]
+            self.ledger.claim(slot, self.ledger.next_start, self.ledger.next_start + (b - a))
+            if transactions is not None:
+                transactions[q].chunk(a, b, copy_bytes=(b - a) * self.bytes_per_token)
             if self.plan.role == "source" and self.transport == "copy_engine":
                 self._send_staged(i, slot, c, st, status)
             elif self.plan.role == "source":
@@ -402,6 +441,10 @@ class TargetPlacement:
                           "cb_chunk_signal")
             self.last_use[slot] = c
             self.counter += 1
+        for slot in range(self.SLOTS):
+            if self.ledger.held[slot]:
+                self.ledger.settle(slot, gpu_reads_complete=True)  # awaited by the next run's device waits
+        self.ledger.close()
         if self.plan.role == "source" and self.transport == "copy_engine":
             # Later work on the caller's stream (the vote) follows every transfer.
             current = torch.cuda.current_stream(self.device)

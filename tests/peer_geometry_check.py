@@ -1,13 +1,13 @@
-"""Byte geometry of a mapped block against fragmented target runs.
+"""Test-side restatement of the reference's peer-copy span geometry.
 
-Drop-in for ``operations`` (src/cachebridge/online/peer_geometry.py:4-54 and
-backends/sglang/runtime/peer_geometry.py:4-54): given the logical token span
-``[start, stop)`` of one mapped block and the request's placement ``runs``
-``(logical_start, logical_stop, physical_start)``, list the copies
-``(kind, layer, src_offset, dst_offset, size)`` that place the block. The
-reference issues one ``cudaMemcpyPeerAsync`` per entry; the B200 path installs
-the same bytes with one kernel launch and uses this list as the placement
-contract it is checked against.
+A checker, not product code: ``operations`` restates
+src/cachebridge/online/peer_geometry.py:4-54 (= backends/sglang/runtime/
+peer_geometry.py:4-54), the byte spans ``(kind, layer, src_offset,
+dst_offset, size)`` that place one mapped block against fragmented target
+runs, with the reference's guards and messages. The B200 path installs the
+same bytes with one kernel launch (``cb_install_rows``); the tests pin this
+restatement to the fixture made by running the reference and use it to check
+that the kernel's placement covers exactly the reference's bytes.
 """
 
 from __future__ import annotations

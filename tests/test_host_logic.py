@@ -14,7 +14,7 @@ from safetensors.torch import save_file
 
 from cachebridge_b200 import PageMapper, contiguous_runs
 from cachebridge_b200.online.blocks import SourceLease, install_unpublished
-from cachebridge_b200.online.peer_geometry import operations
+from peer_geometry_check import operations
 from cachebridge_b200.online.pipeline import PipelinedSourceLease
 from conftest import GOLDEN
 

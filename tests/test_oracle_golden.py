@@ -64,7 +64,7 @@ def test_oracle_contiguous_runs():
 def test_peer_geometry_matches_reference_fixture():
     import hashlib
 
-    from cachebridge_b200.online.peer_geometry import operations
+    from peer_geometry_check import operations
 
     cases = json.loads((GOLDEN / "peer_geometry" / "case.json").read_text())
     for c in cases:

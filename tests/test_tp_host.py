@@ -1,10 +1,14 @@
 """Host logic of the tensor-parallel handoff on CPU: pair plan, chunking, the
-all-rank publication vote and the pool-handle exchange, run as world_size-2
-``gloo`` process groups (no GPU).
+publication transaction (online/transaction.py) and the pool-handle exchange,
+run as world_size-2 ``gloo`` process groups (no GPU).
 
-Failures are made on the host: one rank reports a local error and the vote
-must roll back the transaction on every rank (src/cachebridge/online/blocks.py:114-171,
-backends/sglang/runtime/source_mapper_adapter.py:543-548).
+Failures are made on the host (src/cachebridge/online/blocks.py:114-171,
+backends/sglang/runtime/source_mapper_adapter.py:543-548, :1145-1237): a
+cancellation after k chunks, a foreign rank whose device check fails, a rank
+that cannot certify its GPU work, an identity mismatch, a failed publication,
+and a rank that leaves so that the vote itself fails. Every rank must reach
+the same outcome; freed rows are freed exactly once and quarantined rows
+never.
 """
 
 from __future__ import annotations
@@ -19,6 +23,16 @@ import torch.multiprocessing as mp
 
 from cachebridge_b200.online import tp
 from cachebridge_b200.online.blocks import install_unpublished
+from cachebridge_b200.online.transaction import (
+    PUBLISHED,
+    QUARANTINED,
+    ROLLED_BACK,
+    DeviceDataError,
+    HandoffTransaction,
+    TransactionError,
+    commit,
+    gloo_vote,
+)
 
 
 def test_pair_plan_roles_heads_and_peers():
@@ -51,11 +65,55 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _commit_scenario(rank, scenario):
+    """Two requests per rank; rank 1 is the target (owns rows), rank 0 the source."""
+    freed, published = [], []
+    target = rank == 1
+    ids = ["req-a", "req-b"]
+    if scenario == "identity" and rank == 0:
+        ids = ["req-a", "req-x"]  # this rank commits another request at position 1
+    txns = [HandoffTransaction(rid, 10, rank=rank, allocate=(lambda n: list(range(n))) if target else None,
+                               free=freed.append if target else None,
+                               publish=published.append if target else None,
+                               cancel_after_chunks=2 if (scenario == "cancel" and rank == 0 and i == 0) else None)
+            for i, rid in enumerate(ids)]
+    for t in txns:
+        t.begin()
+        for a, b in tp.chunk_spans(10, 4):
+            t.chunk(a, b, copy_bytes=(b - a) * 64)
+
+    def settle():
+        if scenario == "foreign_device" and rank == 0:
+            raise DeviceDataError("slot outside the pool")
+        if scenario == "uncertified" and rank == 0:
+            raise RuntimeError("stream synchronize failed")
+
+    vote = gloo_vote()
+    if scenario == "publish_fails" and target:
+        def bad_publish(indices):
+            raise RuntimeError("radix insert refused")
+        txns[1].publish = bad_publish
+    if scenario == "vote_broken" and rank == 0:
+        return ("left", 0, 0)  # this rank never votes: the other rank's vote fails
+    try:
+        receipts = commit(txns, settle=settle, vote=vote, expected_ids=["req-a", "req-b"] if rank == 1 else ids)
+        outcome = [r["outcome"] for r in receipts]
+    except TransactionError as exc:
+        outcome = [r["outcome"] for r in exc.receipts]
+    return (outcome, len(freed), len(published))
+
+
 def _worker(rank, world, port, scenario, results):
+    import datetime
+
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    timeout = datetime.timedelta(seconds=5 if scenario == "vote_broken" else 60)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
     try:
+        if scenario.startswith("commit:"):
+            results[rank] = _commit_scenario(rank, scenario.split(":", 1)[1])
+            return
         plan = tp.pair_plan(world, rank, 8)
         if scenario == "vote":
             all_ok = int(tp.publication_vote(True).item())
@@ -86,7 +144,8 @@ def _worker(rank, world, port, scenario, results):
             opened = tp.exchange_target_pools(plan, object() if plan.role == "target" else None)
             results[rank] = opened
     finally:
-        dist.destroy_process_group()
+        if not (scenario == "commit:vote_broken" and rank == 0):
+            dist.destroy_process_group()
 
 
 def _run(scenario, world=2):
@@ -124,3 +183,49 @@ def test_source_rank_opens_its_peer_target_pool():
     res = _run("exchange", world=4)
     assert res[0] == ("pool-of", 2) and res[1] == ("pool-of", 3)
     assert res[2] is None and res[3] is None
+
+
+def test_commit_publishes_when_every_rank_is_ready():
+    res = _run("commit:all_ready")
+    assert res[0] == ([PUBLISHED, PUBLISHED], 0, 0)  # the source owns no rows
+    assert res[1] == ([PUBLISHED, PUBLISHED], 0, 2)
+
+
+def test_commit_rolls_back_a_cancelled_request_on_every_rank():
+    res = _run("commit:cancel")
+    assert res[0][0] == [ROLLED_BACK, PUBLISHED] and res[1][0] == [ROLLED_BACK, PUBLISHED]
+    assert res[1][1:] == (1, 1)  # the target frees the cancelled rows once and publishes the other
+
+
+def test_commit_rolls_back_when_a_foreign_rank_reports_a_device_error():
+    res = _run("commit:foreign_device")
+    for rank in (0, 1):
+        assert res[rank][0] == [ROLLED_BACK, ROLLED_BACK]
+    assert res[1][1:] == (2, 0)
+
+
+def test_commit_quarantines_when_a_rank_cannot_certify_its_gpu_work():
+    res = _run("commit:uncertified")
+    for rank in (0, 1):
+        assert res[rank][0] == [QUARANTINED, QUARANTINED]
+    assert res[1][1:] == (0, 0)  # nothing freed, nothing published: ownership kept
+
+
+def test_commit_rolls_back_on_identity_mismatch():
+    res = _run("commit:identity")
+    for rank in (0, 1):
+        assert res[rank][0] == [PUBLISHED, ROLLED_BACK]
+    assert res[1][1:] == (1, 1)
+
+
+def test_commit_quarantines_a_request_whose_publication_failed():
+    res = _run("commit:publish_fails")
+    for rank in (0, 1):
+        assert res[rank][0] == [PUBLISHED, QUARANTINED]
+    assert res[1][1:] == (0, 1)  # quarantined rows are not freed
+
+
+def test_commit_quarantines_when_the_vote_fails():
+    res = _run("commit:vote_broken")
+    assert res[0] == ("left", 0, 0)
+    assert res[1] == ([QUARANTINED, QUARANTINED], 0, 0)
