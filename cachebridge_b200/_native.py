@@ -29,6 +29,10 @@ CB_INDEX_NONE = 0
 CB_INDEX_I32 = 32
 CB_INDEX_I64 = 64
 
+CB_PATH_CUDA_CORE = 0
+CB_PATH_TENSOR_CORE = 1
+CB_PATH_TENSOR_MEMORY = 2
+
 CB_MAX_LAYERS = 128
 CB_NOALLOC_SCRATCH_BYTES = 64 << 20
 
@@ -42,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "cb_mapper_destroy",
     "cb_mapper_info",
     "cb_mapper_workspace_bytes",
+    "cb_mapper_path",
     "cb_rope_table",
     "cb_map_install",
     "cb_map_install_noalloc",
@@ -125,6 +130,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.cb_mapper_info.argtypes = [c_vp] + [ctypes.POINTER(c_int)] * 5
     lib.cb_mapper_workspace_bytes.restype = c_size
     lib.cb_mapper_workspace_bytes.argtypes = [c_vp, c_int, c_i64]
+    lib.cb_mapper_path.restype = c_int
+    lib.cb_mapper_path.argtypes = [c_vp, c_int, c_i64, c_i64, rope_p, c_int]
     lib.cb_rope_table.restype = c_int
     lib.cb_rope_table.argtypes = [c_vp, rope_p, c_i64, c_i64, c_vp, c_vp, c_i64]
     lib.cb_map_install.restype = c_int

@@ -443,7 +443,9 @@ int launch_tm(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.dst_slot_dtype = dst->slot_dtype;
   p.dst_slots = dst->slots;
   p.dst_evict_first = rows_on_device(m->device, dst) ? 1 : 0;
-  p.dst_v8 = (dst->row_stride * 2) % 32 == 0 ? 1 : 0;
+  // 32-byte stores only into this GPU's own memory; rows of a peer's pool
+  // (stores over NVLink) take 16-byte stores.
+  p.dst_v8 = (p.dst_evict_first && (dst->row_stride * 2) % 32 == 0) ? 1 : 0;
   for (int l = 0; l < dst->layers && p.dst_v8; ++l)
     if (reinterpret_cast<uintptr_t>(dst->k[l]) % 32 || reinterpret_cast<uintptr_t>(dst->v[l]) % 32) p.dst_v8 = 0;
   for (int i = 0; i < 64; ++i) {
@@ -755,6 +757,16 @@ int cb_mapper_info(const cb_mapper* m, int* target_layers, int* heads, int* head
   if (num_selected) *num_selected = m->S;
   if (used_source_layers) *used_source_layers = m->U;
   return CB_OK;
+}
+
+int cb_mapper_path(const cb_mapper* m, int dtype, int64_t n_tokens, int64_t position_start, const cb_rope* dst_rope,
+                   int has_token_order) {
+  if (m == nullptr || dst_rope == nullptr) return fail(CB_ERR_INVALID, "null mapper or RoPE descriptor");
+  if (m->D != cbk::kD || dtype != CB_DTYPE_BF16) return CB_PATH_CUDA_CORE;
+  const int32_t dummy_order = 0;
+  return tm_eligible(m, dst_rope, position_start, n_tokens, has_token_order ? &dummy_order : nullptr)
+             ? CB_PATH_TENSOR_MEMORY
+             : CB_PATH_TENSOR_CORE;
 }
 
 size_t cb_mapper_workspace_bytes(const cb_mapper* m, int dtype, int64_t n_tokens) {

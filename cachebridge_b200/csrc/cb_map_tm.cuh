@@ -60,7 +60,7 @@ struct MapTmParams {
   int dst_slot_dtype;
   const void* dst_slots;
   int dst_evict_first;
-  int dst_v8;                // 1: every destination row is 32-byte aligned (32-byte stores)
+  int dst_v8;                // 1: every destination row is this GPU's and 32-byte aligned (32-byte stores)
 
   // Target RoPE: per frequency i, inv_freq, and the unit rotations by one and
   // by eight positions (cos, sin of inv_freq and 8 inv_freq, from the exact

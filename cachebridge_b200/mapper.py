@@ -251,6 +251,27 @@ class PageMapper:
             pass
 
     # ------------------------------------------------------------------
+    def rope_descriptors(self):
+        """``(source, target)`` ``cb_rope`` descriptors, built once per mapper."""
+        if getattr(self, "_ropes", None) is None:
+            self._ropes = (rope_descriptor(self.head_dim, self.source_rope_theta, self.source_rope_scaling),
+                           rope_descriptor(self.head_dim, self.target_rope_theta, self.target_rope_scaling))
+        return self._ropes
+
+    def kernel_path(self, n_tokens: int, position_start: int = 0, *, dtype=torch.bfloat16, ordered: bool = False) -> str:
+        """Which kernel a map + install call of ``n_tokens`` runs:
+        "tensor_memory" (map_install_tm_kernel), "tensor_core"
+        (map_install_tc_kernel) or "cuda_core" (``cb_mapper_path``)."""
+        code = nat.load().cb_mapper_path(self._handle, storage_dtype_code(dtype), int(n_tokens), int(position_start),
+                                         ctypes.byref(self.rope_descriptors()[1]), int(bool(ordered)))
+        if code < 0:
+            nat.check(code, "cb_mapper_path")
+        return {nat.CB_PATH_CUDA_CORE: "cuda_core", nat.CB_PATH_TENSOR_CORE: "tensor_core",
+                nat.CB_PATH_TENSOR_MEMORY: "tensor_memory"}[code]
+
+    def tensor_memory_path(self, n_tokens: int, position_start: int = 0) -> bool:
+        return self.kernel_path(n_tokens, position_start) == "tensor_memory"
+
     def workspace_bytes(self, dtype: torch.dtype, n_tokens: int) -> int:
         return int(nat.load().cb_mapper_workspace_bytes(self._handle, storage_dtype_code(dtype), int(n_tokens)))
 
@@ -367,8 +388,7 @@ class HandoffCall:
         self.src_c, self.dst_c = src.to_c(), dst.to_c()
         self.dtype = storage_dtype_code(src.dtype)
         self.tensor_core = mapper.head_dim == 128 and src.dtype == torch.bfloat16
-        self.src_rope = rope_descriptor(mapper.head_dim, mapper.source_rope_theta, mapper.source_rope_scaling)
-        self.dst_rope = rope_descriptor(mapper.head_dim, mapper.target_rope_theta, mapper.target_rope_scaling)
+        self.src_rope, self.dst_rope = mapper.rope_descriptors()
         dev = mapper.device
         ws_bytes = mapper.workspace_bytes(src.dtype, n)
         if workspace is None:

@@ -75,6 +75,14 @@ class SlotAllocator:
         self._head = 0  # rows before _head are handed out
         self._live: dict[int, int] = {}  # data_ptr -> length of each live allocation
 
+    @classmethod
+    def from_free_rows(cls, free_rows: torch.Tensor) -> "SlotAllocator":
+        """An allocator over an explicit free list (e.g. a pool whose other
+        rows hold other requests); rows are handed out in the list's order."""
+        alloc = cls(0, device=free_rows.device, seed=None)
+        alloc._free = free_rows.to(torch.int64)
+        return alloc
+
     @property
     def free_rows(self) -> int:
         return self._free.numel() - self._head

@@ -154,6 +154,21 @@ CB_API int cb_mapper_destroy(cb_mapper* mapper);
 CB_API int cb_mapper_info(const cb_mapper* mapper, int* target_layers, int* heads,
                    int* head_dim, int* num_selected, int* used_source_layers);
 /*
+ * Which kernel a map + install call with these arguments runs; no
+ * counterpart in the reference (an introspection helper for callers and
+ * benchmarks). Returns CB_PATH_CUDA_CORE (FP32 storage or head_dim != 128),
+ * CB_PATH_TENSOR_CORE (map_install_tc_kernel: more than four 128-feature
+ * blocks per head, a caller token order, or target-RoPE phases beyond 4e5)
+ * or CB_PATH_TENSOR_MEMORY (map_install_tm_kernel: weights in tensor
+ * memory), or a negative status.
+ */
+#define CB_PATH_CUDA_CORE 0
+#define CB_PATH_TENSOR_CORE 1
+#define CB_PATH_TENSOR_MEMORY 2
+CB_API int cb_mapper_path(const cb_mapper* mapper, int dtype, int64_t n_tokens, int64_t position_start,
+                          const cb_rope* dst_rope, int has_token_order);
+
+/*
  * Bytes of caller-provided scratch that cb_map_install needs for n_tokens
  * tokens of `dtype` storage (0 when the call needs none).
  */

@@ -4,11 +4,14 @@
   - target placement: rank 0 packs raw source rows into rank 1's receive
     slots (staged and moved by the copy engine, or stored straight into the
     peer slot), rank 1 maps them into its own pool (device-side chunk
-    handshake).
-Rank 1 then maps the same inputs locally; the two pools must be
-bit-identical, untouched rows keeping their canary.
+    handshake). Each request is a HandoffTransaction, published by commit
+    (device settle + all-rank host vote).
+The target rank checks every installed row against the CPU oracle (the FP32
+restatement of the reference algorithm, BF16 tolerance of the GPU parity
+tests), every other row against its canary, and, as a cross-check, that a
+local run of the same kernels on the same inputs is bit-identical.
 
-Needs two visible GPUs; skipped otherwise.
+Needs two visible GPUs; skipped otherwise. NVLS is off (peer loads only).
 """
 
 from __future__ import annotations
@@ -86,23 +89,53 @@ def _worker(rank, port, placement, results):
                                       transport=transport, slots=slots)
         # Every rank reaches the vote, a local failure included (it votes 0).
         error = None
-        ready = torch.ones(1, dtype=torch.int32, device=dev)
-        try:
-            if placement == "source" and plan.role == "source":
-                tp.ShardedHandoff(mapper, src_pool, peer, requests, chunk=256).run()
-            elif placement != "source":
-                for _ in range(2):  # two passes: the slot counters carry over
-                    peer.run()
-            ready = tp.device_ready(dev)
-        except Exception as exc:  # noqa: BLE001
-            error = repr(exc)
-            ready = torch.zeros(1, dtype=torch.int32, device=dev)
-        bits = int(status_word(dev).item())  # this rank's device status before the vote
-        vote = int(tp.publication_vote(ready, device=dev).item())
+        if placement == "source":
+            ready = torch.ones(1, dtype=torch.int32, device=dev)
+            try:
+                if plan.role == "source":
+                    tp.ShardedHandoff(mapper, src_pool, peer, requests, chunk=256).run()
+                ready = tp.device_ready(dev)
+            except Exception as exc:  # noqa: BLE001
+                error = repr(exc)
+                ready = torch.zeros(1, dtype=torch.int32, device=dev)
+            bits = int(status_word(dev).item())  # this rank's device status before the vote
+            vote = int(tp.publication_vote(ready, device=dev).item())
+        else:
+            from cachebridge_b200.online.transaction import (HandoffTransaction, TransactionError, commit,
+                                                             device_settle, gloo_vote)
+
+            bits = 0
+            vote = 1
+            for rep in range(2):  # two handoffs: the slot counters carry over
+                txns = [HandoffTransaction(f"req{q}-{rep}", len(s), rank=rank,
+                                           allocate=(lambda n, r=t: r) if plan.role == "target" else None)
+                        for q, (s, t) in enumerate(requests)]
+                for t in txns:
+                    t.begin()
+                try:
+                    peer.run(txns)
+                    receipts = commit(txns, settle=device_settle(dev), vote=gloo_vote(host))
+                    assert all(r["blocks"] == len(tp.chunk_spans(r["tokens"], 256)) for r in receipts)
+                except TransactionError as exc:
+                    error, vote = repr(exc), 0
+                    break
         if vote != 1:  # not published: every rank stops here
             results[rank] = (vote, error, bits)
             return
         if plan.role == "target":
+            from oracle import mapper_oracle as orc
+
+            ref_layers = [dict(selected=t["selected"].tolist(), k_weight=t["k_weight"], k_bias=t["k_bias"],
+                               v_weight=t["v_weight"], v_bias=t["v_bias"]) for t in layers]
+            worst_rel, worst_norm = 0.0, 0.0
+            for s_slots, d_slots in requests:  # each request's history starts at position 0
+                page = torch.stack((src_pool.k_buffer[:, s_slots], src_pool.v_buffer[:, s_slots])).cpu()
+                f32 = orc.map_page_f32(ref_layers, page, position_start=0, head_range=(0, H), source_theta=1e6,
+                                       target_theta=1e6)
+                got = torch.stack((target.k_buffer[:, d_slots], target.v_buffer[:, d_slots])).float().cpu()
+                worst_rel = max(worst_rel, float((got - f32).norm() / f32.norm()))
+                worst_norm = max(worst_norm, float(((got - f32).abs() / f32.abs().clamp_min(1.0)).max()))
+            oracle_ok = worst_rel <= 5e-3 and worst_norm <= 2e-2
             local = cb.TokenKVPool(layers=L_t, rows=rows, heads=H, head_dim=D, device=dev, fill=CANARY)
             tp.ShardedHandoff(mapper, src_pool, local, requests, chunk=256).run()
             torch.cuda.synchronize()
@@ -113,7 +146,7 @@ def _worker(rank, port, placement, results):
             untouched = bool((target.k_buffer[:, mask].float() == CANARY).all()) and bool(
                 (target.v_buffer[:, mask].float() == CANARY).all())
             written = not bool((target.k_buffer[:, dst_perm.to(dev)].float() == CANARY).any())
-            results[rank] = (vote, same, untouched, written)
+            results[rank] = (vote, same, untouched, written, oracle_ok, worst_rel, worst_norm)
         else:
             results[rank] = (vote,)
         if peer is not None:
@@ -146,5 +179,7 @@ def test_sharded_install_is_bit_exact(placement):
         assert codes == [0, 0], f"worker exit codes {codes}"
         res = dict(results)
     assert res[0] == (1,)
-    vote, same, untouched, written = res[1]
-    assert vote == 1 and same and untouched and written
+    vote, same, untouched, written, oracle_ok, rel, norm = res[1]
+    assert vote == 1 and untouched and written
+    assert oracle_ok, f"against the oracle: relative Frobenius {rel:.3e}, normalised max {norm:.3e}"
+    assert same
