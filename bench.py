@@ -916,9 +916,13 @@ def run_sharded(args):
             buf.normal_(generator=gd)
             buf.mul_(torch.exp(0.5 * torch.randn(L_s, 1, Hr, D, generator=gd, device=dev)).to(buf.dtype))
     torch.cuda.synchronize()
+    if args.mixed and mapper is None:  # mixed placement maps some chunks on the source
+        mapper = cb.PageMapper.from_tensors(layers, method="cachebridge", source_rope_theta=theta,
+                                            target_rope_theta=theta, device=dev, target_tp_rank=plan.tp_rank,
+                                            target_tp_size=plan.tp)
     placement = tp.TargetPlacement(plan, requests, chunk=chunk, source_layers=L_s, device=dev, group=host_group,
                                    source_pool=src_pool, mapper=mapper, target_pool=dst_pool,
-                                   transport=args.transport, slots=args.slots)
+                                   transport=args.transport, slots=args.slots, mixed_source_block=args.mixed)
     vote = gloo_vote(host_group)
     settle = device_settle(dev)
 
@@ -1101,7 +1105,8 @@ def run_sharded(args):
                         chunk_tokens=chunk, source_layers=L_s, target_layers=L_t, kv_heads=H, heads_per_rank=Hr,
                         head_dim=D, selected=S, target_pool_slots=rows, page_size=1,
                         target_rows="allocated per handoff from a seeded free list (publication transaction)",
-                        transport_mode=args.transport, receive_slots=args.slots, l2="inputs larger than L2",
+                        transport_mode=args.transport, receive_slots=args.slots, mixed_source_block=args.mixed,
+                        l2="inputs larger than L2",
                         parallelism=f"src tp{plan.tp} -> dst tp{plan.tp}"),
             latency_p50_ms=statistics.median(lat_max),
             latency=dict(what="host clock per handoff, max over ranks: target rows allocated, every chunk queued, "
@@ -1157,6 +1162,8 @@ def main(argv=None):
     ap.add_argument("--chunk", type=int, default=2048, help="tokens per map+install call (N>1)")
     ap.add_argument("--pool-slack", type=int, default=4096, help="free pool rows beyond the requests (N>1)")
     ap.add_argument("--slots", type=int, default=2, help="N>1 target placement: receive slots (chunks in flight)")
+    ap.add_argument("--mixed", choices=["early", "tail"], default=None,
+                    help="N>1: map the first or last chunk of each request on the source (mixed placement)")
     ap.add_argument("--transport", choices=["copy_engine", "peer_stores"], default="peer_stores",
                     help="N>1 target placement: staged chunks moved by the copy engine, or gather-kernel peer stores")
     args = ap.parse_args(argv)

@@ -27,7 +27,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from ..device import RawRows, RowSet, status_word
+from ..device import RawRows, RowSet, install_rows, status_word
 from .transaction import SlotLedger
 
 
@@ -59,6 +59,27 @@ def pair_plan(world: int, rank: int, total_heads: int) -> PairPlan:
     if rank < tp:
         return PairPlan(world, rank, tp, "source", rank, rank + tp, h, rank * h)
     return PairPlan(world, rank, tp, "target", rank - tp, rank - tp, h, (rank - tp) * h)
+
+
+RAW = "raw"        # a chunk crosses NVLink as raw source rows; the target maps it
+MAPPED = "mapped"  # the source maps the chunk; the target installs the mapped rows
+
+
+def mixed_chunk_modes(lengths, chunk: int, source_block: str | None) -> list[str]:
+    """Placement of every chunk of every request (requests in order, chunks
+    in token order). ``source_block`` None maps every chunk on the target;
+    "early" / "tail" map the first / last chunk of each request on the source
+    and the rest on the target (the mixed per-block policy of
+    backends/sglang/runtime/mixed_channel.py:50-104, whose source block index
+    is 0 or the last)."""
+    if source_block not in (None, "early", "tail"):
+        raise ValueError("mixed source block must be None, 'early' or 'tail'")
+    modes = []
+    for n in lengths:
+        spans = chunk_spans(n, chunk)
+        pick = None if source_block is None else (0 if source_block == "early" else len(spans) - 1)
+        modes.extend(MAPPED if i == pick else RAW for i in range(len(spans)))
+    return modes
 
 
 def chunk_spans(n_tokens: int, chunk: int) -> list[tuple[int, int]]:
@@ -273,6 +294,13 @@ class TargetPlacement:
     and native_source.py:29-108, with the double-buffered slots of
     source_mapper_adapter.py:197-232 / 282-324.
 
+    Mixed placement (``mixed_source_block`` "early" or "tail"): one chunk of
+    each request is mapped on the source instead, straight into the receive
+    slot as a dense mapped page (the map kernel's stores go over NVLink), and
+    the target installs it with one row scatter; the receive slots are sized
+    for the larger of the raw and the mapped chunk. The source then needs the
+    ``mapper`` too (peer stores only).
+
     Every rank of the pair builds one with the same ``requests`` (lists of
     ``(source_slots, target_slots)`` device tensors) and ``chunk``; the source
     passes ``source_pool``, the target ``mapper`` and ``target_pool``. The
@@ -287,7 +315,7 @@ class TargetPlacement:
 
     def __init__(self, plan: PairPlan, requests, *, chunk: int, source_layers: int, device: torch.device,
                  group=None, source_pool=None, mapper=None, target_pool=None, timeout_s: float = 10.0,
-                 transport: str = "peer_stores", slots: int = 2):
+                 transport: str = "peer_stores", slots: int = 2, mixed_source_block: str | None = None):
         from .. import _native as nat
         from ..device import storage_dtype_code
 
@@ -302,6 +330,9 @@ class TargetPlacement:
         self.lib = nat.load()
         self.timeout_ns = int(timeout_s * 1e9)
         self.chunks = [(q, a, b) for q, (s, _) in enumerate(requests) for a, b in chunk_spans(len(s), chunk)]
+        self.modes = mixed_chunk_modes([len(s) for s, _ in requests], chunk, mixed_source_block)
+        if mixed_source_block is not None and (mapper is None or transport != "peer_stores"):
+            raise ValueError("mixed placement needs the mapper on both ranks and peer stores")
         self.counter = 0  # chunks enqueued so far, over all runs (the signalled values)
         self.last_use = [-1] * self.SLOTS  # counter of the chunk that last used each slot
         self.status = status_word(self.device)
@@ -315,7 +346,9 @@ class TargetPlacement:
         self.dtype_code = storage_dtype_code(dtype)
         self.head_dim = D
         elem = torch.tensor([], dtype=dtype).element_size()
-        slot_elems = 2 * source_layers * chunk * H * D
+        target_layers = mapper.target_layers if mapper is not None else source_layers
+        layers_in_slot = max(source_layers if RAW in self.modes else 0, target_layers if MAPPED in self.modes else 0)
+        slot_elems = 2 * layers_in_slot * chunk * H * D
         self.slot_bytes = slot_elems * elem
         # Counters start at -1: nothing arrived, nothing consumed.
         flags = torch.full((self.SLOTS,), -1, dtype=torch.int64, device=self.device)
@@ -328,7 +361,7 @@ class TargetPlacement:
         self.flags = flags
         self.ledger = SlotLedger(self.SLOTS, restart_on_open=True)
         self.request_tokens = [len(s) for s, _ in requests]
-        self.bytes_per_token = 2 * source_layers * H * D * elem
+        self.bytes_per_token = {RAW: 2 * source_layers * H * D * elem, MAPPED: 2 * target_layers * H * D * elem}
         torch.cuda.synchronize(self.device)
         gathered = [None] * plan.world
         dist.all_gather_object(gathered, payload, group=group)
@@ -346,9 +379,18 @@ class TargetPlacement:
             self.peer_recv = [recv.ptr + s * self.slot_bytes for s in range(self.SLOTS)]
             self.peer_ready = [ready.ptr + 8 * s for s in range(self.SLOTS)]
             self.src_rows = []
-            for q, a, b in self.chunks:
+            self.src_calls = {}
+            for i, (q, a, b) in enumerate(self.chunks):
                 rs = RowSet.from_pool(source_pool, requests[q][0][a:b])
                 self.src_rows.append((rs, rs.to_c()))
+                if self.modes[i] == MAPPED:
+                    # Map on the source into the peer slot as a dense [2, L_t, n, H, D] page.
+                    n, row = b - a, H * D
+                    base = self.peer_recv[i % self.SLOTS]
+                    page = RawRows([base + l * n * row * elem for l in range(target_layers)],
+                                   [base + (target_layers + l) * n * row * elem for l in range(target_layers)],
+                                   H, D, n, row, dtype, self.device)
+                    self.src_calls[i] = mapper.prepare(rs, page, n, a)
             self.row_heads = source_pool.heads
             self.chunk_bytes = [2 * source_layers * (b - a) * H * D * elem for _, a, b in self.chunks]
             if transport == "copy_engine":
@@ -371,8 +413,15 @@ class TargetPlacement:
             # Each request's target rows, read by its prepared calls.
             self.target_rows = [t.to(self.device, torch.int64).clone() for _, t in requests]
             self.calls = []
+            self.installs = {}
             for i, (q, a, b) in enumerate(self.chunks):
                 n = b - a
+                if self.modes[i] == MAPPED:
+                    # The source mapped this chunk: install the slot's page.
+                    block = self.recv[i % self.SLOTS, : 2 * target_layers * n * H * D].view(2, target_layers, n, H, D)
+                    self.installs[i] = (block, target_pool.rows(self.target_rows[q][a:b]))
+                    self.calls.append(None)
+                    continue
                 page = self.recv[i % self.SLOTS, : 2 * source_layers * n * H * D].view(2, source_layers, n, H, D)
                 self.calls.append(mapper.prepare(RowSet.from_page(page), target_pool.rows(self.target_rows[q][a:b]), n,
                                                  a, workspace=ws))
@@ -381,8 +430,8 @@ class TargetPlacement:
     def launches(self) -> int:
         """Kernel launches per ``run`` on this rank."""
         if self.plan.role == "source":
-            return 3 * len(self.chunks)
-        return sum(4 if c.tensor_core else 3 for c in self.calls)
+            return sum(4 if m == MAPPED else 3 for m in self.modes)
+        return sum(3 if c is None else (4 if c.tensor_core else 3) for c in self.calls)
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -420,23 +469,30 @@ class TargetPlacement:
             q, a, b = self.chunks[i]
             self.ledger.claim(slot, self.ledger.next_start, self.ledger.next_start + (b - a))
             if transactions is not None:
-                transactions[q].chunk(a, b, copy_bytes=(b - a) * self.bytes_per_token)
+                transactions[q].chunk(a, b, copy_bytes=(b - a) * self.bytes_per_token[self.modes[i]])
             if self.plan.role == "source" and self.transport == "copy_engine":
                 self._send_staged(i, slot, c, st, status)
             elif self.plan.role == "source":
                 # The chunk that last used this slot must have been consumed.
                 nat.check(self.lib.cb_chunk_wait(st, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot),
                                                  self.last_use[slot], self.timeout_ns, status), "cb_chunk_wait")
-                rs, crow = self.src_rows[i]
-                nat.check(self.lib.cb_pack_rows(st, ctypes.byref(crow), self.head_dim, self.dtype_code,
-                                                rs.slots.numel(), ctypes.c_void_p(self.peer_recv[slot]), status),
-                          "cb_pack_rows")
+                if self.modes[i] == MAPPED:
+                    self.src_calls[i].run()
+                else:
+                    rs, crow = self.src_rows[i]
+                    nat.check(self.lib.cb_pack_rows(st, ctypes.byref(crow), self.head_dim, self.dtype_code,
+                                                    rs.slots.numel(), ctypes.c_void_p(self.peer_recv[slot]), status),
+                              "cb_pack_rows")
                 nat.check(self.lib.cb_chunk_signal(st, ctypes.c_void_p(self.peer_ready[slot]), c),
                           "cb_chunk_signal")
             else:
                 nat.check(self.lib.cb_chunk_wait(st, ctypes.c_void_p(self.flags.data_ptr() + 8 * slot), c,
                                                  self.timeout_ns, status), "cb_chunk_wait")
-                self.calls[i].run()
+                if self.modes[i] == MAPPED:
+                    block, dst = self.installs[i]
+                    install_rows(block, dst, b - a)
+                else:
+                    self.calls[i].run()
                 nat.check(self.lib.cb_chunk_signal(st, ctypes.c_void_p(self.peer_consumed[slot]), c),
                           "cb_chunk_signal")
             self.last_use[slot] = c

@@ -5,7 +5,10 @@
     slots (staged and moved by the copy engine, or stored straight into the
     peer slot), rank 1 maps them into its own pool (device-side chunk
     handshake). Each request is a HandoffTransaction, published by commit
-    (device settle + all-rank host vote).
+    (device settle + all-rank host vote);
+  - mixed placement: the first ("early") or last ("tail") chunk of each
+    request is mapped on the source into the receive slot and installed by
+    the target, the other chunks as in target placement.
 The target rank checks every installed row against the CPU oracle (the FP32
 restatement of the reference algorithm, BF16 tolerance of the GPU parity
 tests), every other row against its canary, and, as a cross-check, that a
@@ -82,11 +85,12 @@ def _worker(rank, port, placement, results):
         else:
             transport = "copy_engine" if placement == "target_copy_engine" else "peer_stores"
             slots = 3 if placement == "target_3slots" else 2
+            mixed = placement.split("_", 1)[1] if placement.startswith("mixed_") else None
             peer = tp.TargetPlacement(plan, requests, chunk=256, source_layers=L_s, device=dev, group=host,
                                       source_pool=src_pool if plan.role == "source" else None,
-                                      mapper=mapper if plan.role == "target" else None,
+                                      mapper=mapper if (plan.role == "target" or mixed) else None,
                                       target_pool=target if plan.role == "target" else None, timeout_s=20.0,
-                                      transport=transport, slots=slots)
+                                      transport=transport, slots=slots, mixed_source_block=mixed)
         # Every rank reaches the vote, a local failure included (it votes 0).
         error = None
         if placement == "source":
@@ -157,7 +161,8 @@ def _worker(rank, port, placement, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("placement", ["source", "target", "target_copy_engine", "target_3slots"])
+@pytest.mark.parametrize("placement", ["source", "target", "target_copy_engine", "target_3slots", "mixed_early",
+                                       "mixed_tail"])
 def test_sharded_install_is_bit_exact(placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

@@ -59,6 +59,15 @@ def test_chunk_spans_are_ordered_and_gap_free():
         tp.chunk_spans(10, 0)
 
 
+def test_mixed_chunk_modes_put_one_chunk_per_request_on_the_source():
+    lengths = [5000, 2048, 100]
+    assert tp.mixed_chunk_modes(lengths, 2048, None) == [tp.RAW] * 5
+    assert tp.mixed_chunk_modes(lengths, 2048, "early") == [tp.MAPPED, tp.RAW, tp.RAW, tp.MAPPED, tp.MAPPED]
+    assert tp.mixed_chunk_modes(lengths, 2048, "tail") == [tp.RAW, tp.RAW, tp.MAPPED, tp.MAPPED, tp.MAPPED]
+    with pytest.raises(ValueError, match="mixed source block"):
+        tp.mixed_chunk_modes(lengths, 2048, "middle")
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
