@@ -173,10 +173,27 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const __grid_constant__ 
       for (int r = 0; r < RPW; ++r)
         if (src[r] != nullptr && lane < nvec) reinterpret_cast<V*>(dst[r])[lane] = v[r];
     } else {
+      // Long rows: four vectors per lane in flight, all loaded before any is
+      // stored (the stores could otherwise alias the next loads and serialise
+      // them behind one another).
 #pragma unroll
       for (int r = 0; r < RPW; ++r) {
         if (src[r] == nullptr) continue;
-        for (int e = lane; e < nvec; e += 32) reinterpret_cast<V*>(dst[r])[e] = reinterpret_cast<const V*>(src[r])[e];
+        const V* s = reinterpret_cast<const V*>(src[r]);
+        V* d = reinterpret_cast<V*>(dst[r]);
+        for (int e0 = 0; e0 < nvec; e0 += 128) {
+          V v[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e = e0 + lane + 32 * i;
+            if (e < nvec) v[i] = s[e];
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e = e0 + lane + 32 * i;
+            if (e < nvec) d[e] = v[i];
+          }
+        }
       }
     }
   }
