@@ -265,6 +265,25 @@ def test_pack_source_block_matches_reference(cuda_device):
         pack_source_block(pool, indices, start=0, stop=4, workspace=workspace[:-1], block_tokens=512)
 
 
+@pytest.mark.parametrize("heads", [2, 3, 8, 16])
+def test_pack_rows_of_every_length_is_a_gather(cuda_device, heads):
+    """Row gather of pools whose rows are 512 B (four rows per warp), 768 B
+    (a ragged vector count), 2 KB and 4 KB (several rounds of four vectors
+    per lane): bit-identical to the torch gather of the same slots."""
+    g = torch.Generator().manual_seed(heads)
+    layers, rows, n = 5, 3000, 777
+    pool = TokenKVPool(layers=layers, rows=rows, heads=heads, head_dim=128, device=cuda_device)
+    pool.k_buffer.normal_(generator=torch.Generator(device=cuda_device).manual_seed(heads))
+    pool.v_buffer.normal_(generator=torch.Generator(device=cuda_device).manual_seed(heads + 1))
+    indices = torch.randperm(rows, generator=g)[:n].to(cuda_device)
+    workspace = torch.empty(2 * layers * n * heads * 128, dtype=torch.bfloat16, device=cuda_device)
+    packed = pack_source_block(pool, indices, start=0, stop=n, workspace=workspace, block_tokens=n)
+    torch.cuda.synchronize()
+    raise_for_status(cuda_device)
+    ref = torch.stack((pool.k_buffer[:, indices], pool.v_buffer[:, indices]))
+    assert torch.equal(packed.reshape(ref.shape), ref)
+
+
 def test_install_codec_places_rows_bit_exactly(cuda_device):
     g = torch.Generator().manual_seed(21)
     layers, heads, D, n = 64, 2, 128, 700
