@@ -57,6 +57,9 @@ class RowSet:
     head_offset: int = 0
     slots: torch.Tensor | None = None
     _keep: list = field(default_factory=list, repr=False)
+    # Validated layer geometry of a pool (from_pool): the row stride and the C
+    # pointer arrays, shared by every RowSet of that pool.
+    _layers_c: "_PoolLayers | None" = field(default=None, repr=False)
 
     @property
     def layers(self) -> int:
@@ -76,11 +79,8 @@ class RowSet:
 
     @staticmethod
     def from_pool(pool, slots=None, head_offset: int = 0) -> "RowSet":
-        layers = range(pool.start_layer, pool.start_layer + pool.layer_num)
-        k = [pool._get_key_buffer(l) for l in layers]
-        v = [pool._get_value_buffer(l) for l in layers]
-        heads, dim = k[0].shape[1:]
-        return RowSet(k, v, int(heads), int(dim), head_offset, slots)
+        pl = _pool_layers(pool)
+        return RowSet(pl.k, pl.v, pl.heads, pl.head_dim, head_offset, slots, _layers_c=pl)
 
     @staticmethod
     def from_page(page: torch.Tensor, head_offset: int = 0) -> "RowSet":
@@ -109,19 +109,28 @@ class RowSet:
                 stride = t.stride(0)
             elif t.stride(0) != stride:
                 raise ValueError("pool layers must share one row stride")
+        self._validate_slots()
+        return int(stride)
+
+    def _validate_slots(self) -> None:
         if self.slots is not None:
             require_cuda(self.slots, "slot indices")
             if self.slots.ndim != 1:
                 raise ValueError("one-dimensional integer pool indices required")
             if not self.slots.is_contiguous():
                 self.slots = self.slots.contiguous()
-        return int(stride)
 
     def to_c(self) -> nat.CbRows:
-        stride = self.validate()
-        karr = nat.pointer_array([t.data_ptr() for t in self.k])
-        varr = nat.pointer_array([t.data_ptr() for t in self.v])
-        self._keep.extend([karr, varr])
+        pl = self._layers_c
+        if pl is not None and pl.k is self.k and pl.v is self.v:
+            # A pool's layers, validated once when their views were cached.
+            self._validate_slots()
+            stride, karr, varr = pl.row_stride, pl.karr, pl.varr
+        else:
+            stride = self.validate()
+            karr = nat.pointer_array([t.data_ptr() for t in self.k])
+            varr = nat.pointer_array([t.data_ptr() for t in self.v])
+            self._keep.extend([karr, varr])
         return nat.CbRows(
             layers=self.layers,
             heads=self.heads,
@@ -133,6 +142,45 @@ class RowSet:
             slot_dtype=slot_code(self.slots),
             slots=None if self.slots is None else self.slots.data_ptr(),
         )
+
+
+@dataclass
+class _PoolLayers:
+    """A pool's per-layer K/V views with their validated row stride and C
+    pointer arrays. Building these walks every layer of the pool in Python
+    (two views, a dozen attribute checks and a pointer per layer and kind,
+    about 0.3 ms for a 64-layer pool), which a handoff would otherwise repeat
+    for every chunk it maps; they are built once per pool and rebuilt only
+    when its first layer's buffer moves."""
+
+    key: tuple
+    k: list
+    v: list
+    heads: int
+    head_dim: int
+    row_stride: int
+    karr: ctypes.Array
+    varr: ctypes.Array
+
+
+def _pool_layers(pool) -> _PoolLayers:
+    first = pool._get_key_buffer(pool.start_layer)
+    key = (pool.start_layer, pool.layer_num, first.data_ptr(), tuple(first.shape), first.dtype, first.device)
+    cached = getattr(pool, "_cb_pool_layers", None)
+    if cached is not None and cached.key == key:
+        return cached
+    layers = range(pool.start_layer, pool.start_layer + pool.layer_num)
+    k = [pool._get_key_buffer(l) for l in layers]
+    v = [pool._get_value_buffer(l) for l in layers]
+    heads, dim = k[0].shape[1:]
+    stride = RowSet(k, v, int(heads), int(dim)).validate()
+    pl = _PoolLayers(key, k, v, int(heads), int(dim), stride, nat.pointer_array([t.data_ptr() for t in k]),
+                     nat.pointer_array([t.data_ptr() for t in v]))
+    try:
+        pool._cb_pool_layers = pl
+    except AttributeError:  # a pool type that takes no new attributes: rebuilt per call
+        pass
+    return pl
 
 
 @dataclass

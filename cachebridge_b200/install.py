@@ -39,10 +39,19 @@ class DirectMappedPoolCodec:
         self.pool = pool
         self.indices = indices
         self.head_offset = int(head_offset)
-        self.runs = contiguous_runs(indices.detach().cpu().tolist())
+        self._runs = None
         self.start = None
         self.stop = None
         self.install_stream = torch.cuda.Stream(device=self.device)
+
+    @property
+    def runs(self) -> list[tuple[int, int, int]]:
+        """``contiguous_runs`` of the slot list (for receipts). Computed on first
+        use: it copies the indices to the host, which the install itself
+        never needs."""
+        if self._runs is None:
+            self._runs = contiguous_runs(self.indices.detach().cpu().tolist())
+        return self._runs
 
     @property
     def workspace_bytes(self) -> int:
