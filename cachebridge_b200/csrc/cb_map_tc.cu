@@ -76,19 +76,6 @@ struct Smem {
 
 __device__ __forceinline__ uint32_t bar_at(const Smem& s, int idx) { return s.bars + 8u * idx; }
 
-// UMMA descriptor of one K=16 step of a 128-row K-major operand without
-// swizzle: 8-row x 16-byte core matrices, the two K halves 128 B apart
-// (leading byte offset), consecutive 8-row groups 256 B apart (stride byte
-// offset). Element (row r, k) sits at (r/8)*256 + (k/8)*128 + (r%8)*16 + (k%8)*2.
-__device__ __forceinline__ uint64_t make_noswizzle_k16_desc(uint32_t smem_addr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(128u >> 4) << 16;
-  d |= static_cast<uint64_t>(256u >> 4) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  return d;  // layout type 0: no swizzle
-}
-
 // cos and sin of an FP32 phase up to a sign: Cody-Waite reduction by pi
 // (k = rint(phi / pi); r = phi - k*P1 - k*P2 with P1 = fl(pi) and
 // P2 = fl(pi - P1); phi - k*P1 is exact inside the FMA), then the hardware

@@ -5,8 +5,10 @@
 // For every target layer l, target head h, kind (K or V) and 128-token tile,
 //     D^T = W^T . X^T      (D^T: 128 output features x 128 tokens, FP32 in TMEM)
 // with X the concatenation of the S selected source layers' rows of head h
-// (src/cachebridge/mapper.py:153-181). The epilogue adds the FP32 bias, applies
-// the target RoPE to keys (mapper.py:207-239), rounds to BF16 and stores each
+// (src/cachebridge/mapper.py:153-181). Each tile starts with one K=16 step that
+// writes the bias into the accumulator (the unit's [bias_hi, bias_lo] block,
+// the FP32 bias split into two BF16 parts, times a constant ones block); the
+// epilogue applies the target RoPE to keys (mapper.py:207-239), rounds to BF16 and stores each
 // 256-byte head row into the target pool row dst_slots[t]
 // (online/blocks.py:86-111 set_kv_buffer; source_mapper_adapter.py:389-425).
 //
@@ -37,9 +39,11 @@
 //                group meet on mbarriers (bounded waits), not bar.sync, so a
 //                warp that gives up cannot leave the others blocked.
 //   warp 12      TMEM owner + single-thread tcgen05.mma issuer (M=128, N=128,
-//                K=16, A from tensor memory).
+//                K=16, A from tensor memory; the bias step reads A and B from
+//                shared memory).
 //   warps 13-16  weight loaders: 16-byte loads of the unit's pre-arranged image,
-//                tcgen05.st into the weight buffer (one warp per lane quarter).
+//                tcgen05.st into the weight buffer (one warp per lane quarter),
+//                and the [bias_hi, bias_lo] rows of the buffer's bias block.
 // Every wait is bounded (kWaitTimeoutNs): an expired wait flags
 // CB_DEV_ERR_TIMEOUT and the CTA unwinds instead of hanging.
 #include "cb_device.cuh"
@@ -65,6 +69,8 @@ constexpr int kMaxStages = 8;
 struct Smem {
   uint32_t a;        // token-tile stages
   uint32_t stage;    // epilogue staging tiles (shared::cta address)
+  uint32_t bias;     // bias blocks, one per weight buffer (no-swizzle K=16 layout)
+  uint32_t ones;     // constant ones block of the bias step
   uint8_t* stage_gen;
   uint32_t bars;
   uint32_t* tmem_holder;
@@ -159,6 +165,17 @@ __device__ void run_weight_loader(const MapTmParams& p, const Smem& s, uint32_t 
       }
       tmem_st_32x32b_x32(taddr + h8 * 32, v);
     }
+    {
+      // Row L of the buffer's bias block: [bias_hi, bias_lo] of output
+      // feature f(L) at k = 0, 1 (the rest of the block stays zero).
+      const float b = __ldg(p.bias + static_cast<int64_t>((it.kind * p.L_t + it.l) * p.H + it.h) * kD +
+                            tm_lane_feature(L));
+      const float hi = __bfloat162float(__float2bfloat16_rn(b));
+      const uint32_t word = pack_bf16x2(hi, __fsub_rn(b, hi));
+      const uint32_t addr = s.bias + wb * kBiasBlockBytes + (L >> 3) * 256 + (L & 7) * 16;
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
+      fence_proxy_async_smem();  // read by the MMA (async proxy)
+    }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -170,6 +187,7 @@ __device__ void run_weight_loader(const MapTmParams& p, const Smem& s, uint32_t 
 __device__ void run_mma(const MapTmParams& p, const Smem& s, uint32_t tmem_base) {
   constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, kBM);  // M = 128 features, N = 128 tokens
   const uint64_t b_desc0 = make_sw128_kmajor_desc(s.a);
+  const uint64_t ones_desc = make_noswizzle_k16_desc(s.ones);
   constexpr uint64_t kBlockDesc = kKBlockBytes >> 4;
   const int NS = p.stages;
   const int WB = p.w_bufs;
@@ -192,6 +210,8 @@ __device__ void run_mma(const MapTmParams& p, const Smem& s, uint32_t tmem_base)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * kTmAccCols;
+      // Accumulator := [bias_hi, bias_lo] @ ones[:, 0:2]^T = the bias of each feature row.
+      umma_bf16(d_tmem, make_noswizzle_k16_desc(s.bias + wb * kBiasBlockBytes), ones_desc, idesc, 0u);
       for (int kb = 0; kb < p.KB; ++kb) {
         if (!mbar_wait(bar_at(s, kBarFull + stage), phase, s.abort_flag, p.status)) {
           ok = false;
@@ -205,7 +225,7 @@ __device__ void run_mma(const MapTmParams& p, const Smem& s, uint32_t tmem_base)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t off = static_cast<uint64_t>((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
-          umma_bf16_ts(d_tmem, a_base + kb * 64 + kk * 8, bd + off, idesc, (kb | kk) ? 1u : 0u);
+          umma_bf16_ts(d_tmem, a_base + kb * 64 + kk * 8, bd + off, idesc, 1u);
         }
         umma_commit(bar_at(s, kBarEmpty + stage));
         if (++stage == NS) {
@@ -328,15 +348,6 @@ __device__ void run_epilogue(const MapTmParams& p, const Smem& s, uint32_t tmem_
         row_ptr = reinterpret_cast<char*>(it.kind ? p.dst_v[it.l] : p.dst_k[it.l]) +
                   static_cast<int64_t>(p.dst_head_offset + it.h) * (kD * 2) + slot * dst_stride_bytes;
     }
-    // Bias of this thread's four features (FP32, as the reference adds it).
-    const float* bias = p.bias + static_cast<int64_t>((it.kind * p.L_t + it.l) * p.H + it.h) * kD;
-    float b_lo[2], b_hi[2];
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      const int i = 8 * (2 * q + b) + j;
-      b_lo[b] = __ldg(bias + i);
-      b_hi[b] = __ldg(bias + 64 + i);
-    }
     const bool rope = it.kind == 0;
     const int tile_tok0 = it.tok0 + cur.m * kBM;
     const float pos0 = static_cast<float>(p.position_start + tile_tok0 + 2 * quad);
@@ -380,10 +391,10 @@ __device__ void run_epilogue(const MapTmParams& p, const Smem& s, uint32_t tmem_
       for (int b = 0; b < 2; ++b) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          float y0a = __fadd_rn(__uint_as_float(r[b][4 * k + 0]), b_lo[b]);  // feature i, token 2quad + 8k
-          float y0b = __fadd_rn(__uint_as_float(r[b][4 * k + 1]), b_lo[b]);  // feature i, token + 1
-          float y1a = __fadd_rn(__uint_as_float(r[b][4 * k + 2]), b_hi[b]);  // feature i + 64
-          float y1b = __fadd_rn(__uint_as_float(r[b][4 * k + 3]), b_hi[b]);
+          float y0a = __uint_as_float(r[b][4 * k + 0]);  // feature i, token 2quad + 8k
+          float y0b = __uint_as_float(r[b][4 * k + 1]);  // feature i, token + 1
+          float y1a = __uint_as_float(r[b][4 * k + 2]);  // feature i + 64
+          float y1b = __uint_as_float(r[b][4 * k + 3]);
           if (rope) {
             const float pa = pos0 + static_cast<float>(32 * c + 8 * k);
             const float ca = rt[b].c, sa = rt[b].s;
@@ -475,7 +486,9 @@ __global__ void __launch_bounds__(kTmThreads, 1) map_install_tm_kernel(const __g
   s.a = base;
   s.stage = s.a + p.stages * kKBlockBytes;
   s.stage_gen = base_gen + (s.stage - base);
-  s.bars = s.stage + kTmEpiGroups * kTmStageBytes;
+  s.bias = s.stage + kTmEpiGroups * kTmStageBytes;
+  s.ones = s.bias + 2 * kBiasBlockBytes;
+  s.bars = s.ones + kOnesBytes;
   uint8_t* bars_gen = base_gen + (s.bars - base);
   s.tmem_holder = reinterpret_cast<uint32_t*>(bars_gen + 8 * kNumBars);
   s.abort_flag = reinterpret_cast<volatile int*>(bars_gen + 8 * kNumBars + 4);
@@ -502,6 +515,19 @@ __global__ void __launch_bounds__(kTmThreads, 1) map_install_tm_kernel(const __g
     // A device timeout before this launch: every role skips its work.
     *s.abort_flag = status_timed_out(p.status) ? 1 : 0;
     fence_mbarrier_init();
+  }
+  // Constant operands of the bias step: the ones block (rows of [1, 1, 0 x 14])
+  // and two bias blocks whose rows the loaders fill at k = 0, 1 (zero elsewhere).
+  // No-swizzle K=16 layout: element (row r, k) at (r/8)*256 + (k/8)*128 + (r%8)*16 + (k%8)*2.
+  {
+    uint16_t* ones = reinterpret_cast<uint16_t*>(base_gen + (s.ones - base));
+    uint16_t* bias = reinterpret_cast<uint16_t*>(base_gen + (s.bias - base));
+    for (int idx = threadIdx.x; idx < kOnesBytes / 2; idx += blockDim.x) {
+      const int kidx = ((idx >> 6) & 1) * 8 + (idx & 7);  // (byte/128 % 2) * 8 + byte%16/2
+      ones[idx] = kidx < 2 ? static_cast<uint16_t>(0x3F80) : static_cast<uint16_t>(0);
+    }
+    for (int idx = threadIdx.x; idx < kBiasBlockBytes; idx += blockDim.x) bias[idx] = 0;  // both blocks
+    fence_proxy_async_smem();
   }
   if (warp == kTmMmaWarp) {
     tmem_alloc(smem_u32(s.tmem_holder), 512);

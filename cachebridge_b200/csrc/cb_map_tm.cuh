@@ -41,7 +41,7 @@ struct MapTmParams {
   // memory lanes L and L + 8 hold the RoPE pair (i, i + 64).
   const uint8_t* w_tm;
   int64_t unit_bytes;        // KB * 32 KB
-  const float* bias;         // [2][L_t][H][128] FP32
+  const float* bias;         // [2][L_t][H][128] FP32 (split into BF16 hi + lo for the bias step)
   const int* sel_global;     // [L_t][S]
   const int* sel_local;      // [L_t][S]
 
@@ -76,7 +76,10 @@ struct MapTmParams {
 
 __global__ void map_install_tm_kernel(const __grid_constant__ MapTmParams p);
 
-constexpr int kTmFixedSmem = 1024 /* alignment */ + kTmEpiGroups * kTmStageBytes + 512 /* barriers */;
+// Fixed shared memory: staging tiles, two bias blocks (one per weight buffer)
+// and the constant ones block of the bias step, barriers.
+constexpr int kTmFixedSmem =
+    1024 /* alignment */ + kTmEpiGroups * kTmStageBytes + 2 * kBiasBlockBytes + kOnesBytes + 512 /* barriers */;
 
 inline int tm_smem_bytes(int stages) { return kTmFixedSmem + stages * kKBlockBytes; }
 
