@@ -31,7 +31,7 @@
 //                n with n % 2 == g (accumulator g). Warp w reads TMEM lane
 //                quarter w % 4 with tcgen05.ld.16x256b, whose fragment gives
 //                each thread lanes (j, j + 8) of a 16-lane block, i.e. one
-//                RoPE pair, at two adjacent token columns. Bias, RoPE and BF16
+//                RoPE pair, at two adjacent token columns. RoPE and BF16
 //                packing in registers; stmatrix .trans writes token rows into
 //                a 128-row staging tile per group (272-byte row pitch: whole
 //                rows, no bank conflicts); each warp then stores 32 rows, two
