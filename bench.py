@@ -254,7 +254,7 @@ def reprefill_estimate(device, *, tokens, requests, tp, reps=3):
 # ----------------------------------------------------------------------------
 # The reference's torch path on this GPU (the baseline the fused kernels replace)
 # ----------------------------------------------------------------------------
-def reference_map_fp32(layers, block, *, theta, position_start=0):
+def reference_map_fp32(layers, block, *, theta, position_start=0, bf16_keys=False):
     """The reference's PageMapper.map_page on a packed block, before its cast.
 
     ``block`` is ``[2, L_s, n, H, D]`` (keys RoPE-applied, any device). RoPE is
@@ -263,7 +263,9 @@ def reference_map_fp32(layers, block, *, theta, position_start=0):
     layer the selected layers are concatenated along features and mapped with
     einsum('thf,hfd->thd') and the FP32 weights plus bias (mapper.py:153-181);
     the keys get the target RoPE (mapper.py:207-239). Returns FP32
-    ``[2, L_t, n, H, D]``.
+    ``[2, L_t, n, H, D]``. ``bf16_keys`` rounds the derotated keys to BF16
+    before the einsum, as the kernels do with their tensor-core operand (the
+    reference keeps them in FP32); it measures that one rounding on its own.
     """
     dev = block.device
     n, D = block.shape[2], block.shape[4]
@@ -278,6 +280,8 @@ def reference_map_fp32(layers, block, *, theta, position_start=0):
 
     keys = block[0].float()
     keys = (keys * cos - rot(keys) * sin) / torch.clamp_min(cos * cos + sin * sin, torch.finfo(torch.float32).tiny)
+    if bf16_keys:
+        keys = keys.to(torch.bfloat16).float()
     values = block[1].float()
     out_k, out_v = [], []
     for t in layers:
@@ -560,7 +564,19 @@ def run_single(args):
     f32 = reference_map_fp32(layers, block, theta=theta, position_start=0)
     ours = torch.stack((dst_pool.k_buffer[:, dst_slots], dst_pool.v_buffer[:, dst_slots]))
     values = value_parity(ours, f32)
-    del block, f32, ours, mask
+    del ours
+    # The kernels' one rounding step the reference does not have: derotated
+    # keys rounded to BF16 before the GEMM. The same FP32 algorithm with only
+    # that rounding added, against the FP32 result, on the mapped keys.
+    f32_k = reference_map_fp32(layers, block, theta=theta, position_start=0, bf16_keys=True)[0]
+    dk = f32_k - f32[0]
+    key_rounding = dict(max_abs=float(dk.abs().max()),
+                        rel_frobenius=float(dk.double().norm() / f32[0].double().norm().clamp_min(1e-30)),
+                        ref_bf16_max_abs_keys=float((f32[0].to(torch.bfloat16).float() - f32[0]).abs().max()),
+                        what="FP32 reference with the derotated keys rounded to BF16 before the einsum, "
+                             "against the FP32 reference (mapped keys, all tokens, layers and heads)")
+    values["key_rounding"] = key_rounding
+    del block, f32, f32_k, dk, mask
     torch.cuda.empty_cache()
     parity = dict(placement=placement, values=values, ok=bool(placement["ok"] and values["ok"]),
                   scope=f"all {n} tokens x {L_t} layers x {H} heads x K/V against the FP32 restatement of the "
