@@ -37,7 +37,9 @@ __global__ void rope_table_kernel(const __grid_constant__ RopeTableParams p) {
 // ---------------------------------------------------------------------------
 // Key gather + source-RoPE removal -> BF16 content-space workspace
 // ---------------------------------------------------------------------------
-// One warp per token. Lane = (row group g = lane/8, pair index j = lane%8):
+// One warp per (token, part): the U*H rows of a token are split into `parts`
+// runs of rows_per_part so that small calls still fill the GPU. Lane = (row
+// group g = lane/8, pair index j = lane%8):
 // it owns elements [8j, 8j+8) and [64+8j, 64+8j+8) of one 128-wide head row,
 // i.e. 8 complete RoPE pairs, so the rotation needs no data exchange. Four
 // consecutive heads of the same slot row are read per warp instruction (1 KB
@@ -51,7 +53,9 @@ __global__ void rope_table_kernel(const __grid_constant__ RopeTableParams p) {
 __global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_constant__ DerotateParams p) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  const int64_t wg = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+  const int64_t t = wg / p.parts;
+  const int part = static_cast<int>(wg - t * p.parts);
   if (t >= p.n_tokens || status_timed_out(p.status)) return;
   const int g = lane >> 3;
   const int j = lane & 7;
@@ -76,10 +80,11 @@ __global__ void __launch_bounds__(256, 3) derotate_pack_kernel(const __grid_cons
       s[e] = __fmul_rn(s[e], inv);
     }
   }
-  const int rows = p.U * p.H;
+  const int r_begin = part * p.rows_per_part;
+  const int rows = min(p.U * p.H, r_begin + p.rows_per_part);  // end of this warp's rows
   const int64_t src_off = slot * p.src_row_stride;
   constexpr int kUnroll = 4;
-  for (int r0 = 0; r0 < rows; r0 += 4 * kUnroll) {
+  for (int r0 = r_begin; r0 < rows; r0 += 4 * kUnroll) {
     uint4 a[kUnroll], b[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {

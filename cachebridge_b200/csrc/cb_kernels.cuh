@@ -31,6 +31,8 @@ struct DerotateParams {
   int64_t position_start;
   const int32_t* order;  // processing order of the tokens, or null
   __nv_bfloat16* ws;  // [U][n][H][128], rows in processing order
+  int parts;          // warps per token: part p takes rows [p, p + 1) * rows_per_part of its U*H
+  int rows_per_part;  // a multiple of 16
   int32_t* status;
 };
 
