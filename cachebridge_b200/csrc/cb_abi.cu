@@ -308,13 +308,19 @@ bool needs_exact_trig(const cb_rope* dst_rope, int64_t position_start, int64_t n
 // source layer) then stay within one 1024-token window, so a row's later
 // readers find it in L2. Measured at the 8192-token Qwen3 shapes: runs of 64
 // / 32 / 16 / 8 m-tiles take 1.099 / 1.089 / 1.077 / 1.070 ms.
+// The tensor-memory kernel with a single weight buffer (S >= 3) reloads its
+// weights between items with the MMA stalled, and those reloads are about a
+// tenth of its L2 -> shared-memory bytes: it takes runs of up to 32 m-tiles
+// (one 16384-token config-4 request: 3.82 -> 3.43 ms; config 2, double
+// buffered, unchanged at any cap).
 constexpr int64_t kMaxRunMtiles = 8;
+constexpr int64_t kMaxRunMtilesOneWeightBuffer = 32;
 
-int tc_chunk_mtiles(int64_t n_tokens, int64_t groups, int grid) {
+int tc_chunk_mtiles(int64_t n_tokens, int64_t groups, int grid, int64_t max_run = kMaxRunMtiles) {
   const int64_t mt = (n_tokens + cbk::kBM - 1) / cbk::kBM;
   int best_r = 1;
   int64_t best_cost = -1;
-  for (int64_t r = 1; r <= mt && r <= kMaxRunMtiles; ++r) {
+  for (int64_t r = 1; r <= mt && r <= max_run; ++r) {
     const int64_t items = groups * ((mt + r - 1) / r);
     const int64_t cost = ((items + grid - 1) / grid) * (r + 5);
     if (best_cost < 0 || cost <= best_cost) {
@@ -416,15 +422,16 @@ int launch_tm(const cb_mapper* m, cudaStream_t st, const cb_rows* src, const cb_
   p.KB = m->KB;
   p.kb_heads = m->Hs > 0 ? m->Hs : 1;
   p.dense = m->Hs > 0 ? 1 : 0;
-  p.R = tc_chunk_mtiles(n_tokens, 2ll * m->H * m->L_t, m->num_sms);
+  // Two weight buffers when both fit beside the accumulators (S <= 2).
+  p.w_bufs = (512 - cbk::kTmWeightCol0) / (64 * m->KB) >= 2 ? 2 : 1;
+  p.R = tc_chunk_mtiles(n_tokens, 2ll * m->H * m->L_t, m->num_sms,
+                        p.w_bufs == 1 ? kMaxRunMtilesOneWeightBuffer : kMaxRunMtiles);
   p.n_chunks = static_cast<int>((n_tokens + p.R * cbk::kBM - 1) / (p.R * cbk::kBM));
   const int64_t items = 2ll * m->H * p.n_chunks * m->L_t;
   if (items > (int64_t(1) << 31) - 1) return fail(CB_ERR_UNSUPPORTED, "work too large for one call");
   p.num_items = static_cast<int>(items);
   p.stages = std::min(8, (cbk::kTcMaxSmem - cbk::tm_smem_bytes(0)) / cbk::kKBlockBytes);
   if (p.stages < 2) return fail(CB_ERR_UNSUPPORTED, "shared memory too small for the pipeline");
-  // Two weight buffers when both fit beside the accumulators (S <= 2).
-  p.w_bufs = (512 - cbk::kTmWeightCol0) / (64 * m->KB) >= 2 ? 2 : 1;
   p.w_tm = m->w_tm;
   p.unit_bytes = static_cast<int64_t>(m->KB) * cbk::kKBlockBytes;
   p.bias = m->b32;
