@@ -752,7 +752,7 @@ def run_cfg4(args, dev):
 
     c = LLAMA
     L_s, L_t, H, D, S, theta, ps = (c[k] for k in ("L_s", "L_t", "H", "D", "S", "theta", "page_size"))
-    n, nreq = c["tokens"], c["requests"]
+    n, nreq = args.cfg4_tokens, args.cfg4_requests
     pages = 2 * nreq * n // ps
     rows = pages * ps
     layers = random_layers(L_s=L_s, L_t=L_t, H=H, D=D, S=S, seed=13)
@@ -796,7 +796,8 @@ def run_cfg4(args, dev):
     cb.raise_for_status(dev)
     # Parity of request 0 against the FP32 restatement on a 2048-token window,
     # and placement of its rows (the other requests' rows are still canary).
-    a, b = 4096, 4096 + 2048
+    a = min(4096, n // 2)
+    b = min(a + 2048, n)
     block = torch.stack((src_pool.k_buffer[:, src[0][a:b]], src_pool.v_buffer[:, src[0][a:b]]))
     f32 = reference_map_fp32(layers, block, theta=theta, position_start=a)
     ours = torch.stack((dst_pool.k_buffer[:, dst[0][a:b]], dst_pool.v_buffer[:, dst[0][a:b]]))
@@ -818,7 +819,7 @@ def run_cfg4(args, dev):
     tc_sust = measured_peak("bf16_tflops_sustained", 1400.0)
     tflops = flops / (step_ms / 1e3) / 1e12
     out = dict(
-        workload="llama-3.1-8b->70b handoff (BASELINE config 4): 4 x 16384 tokens, 32 -> 80 layers, 8 heads, S=4, "
+        workload=f"llama-3.1-8b->70b handoff (BASELINE config 4): {nreq} x {n} tokens, 32 -> 80 layers, 8 heads, S=4, "
                  "page_size 16, pages from a seeded shuffled free-page list", tokens_per_step=tokens,
         value=tokens / (step_ms / 1e3), unit=UNIT, ms_per_step=step_ms,
         kernels_ms=dict(derotate_pack=pre_ms, map_install=map_ms,
@@ -831,7 +832,7 @@ def run_cfg4(args, dev):
                       algorithmic_bytes=bytes_alg, hbm_gbs=bytes_alg / (step_ms / 1e3) / 1e9,
                       hbm_roofline_ms=1e3 * bytes_alg / (hbm_peak * 1e9)),
         parity=dict(values=values, placement=placement, ok=bool(values["ok"] and placement["ok"]),
-                    scope="request 0: tokens 4096..6143 x 80 layers x 8 heads x K/V against the FP32 restatement; "
+                    scope=f"request 0: tokens {a}..{b - 1} x 80 layers x 8 heads x K/V against the FP32 restatement; "
                           "every pool row against its canary after request 0's install"),
     )
     log(f"config 4: {json.dumps(out)[:400]}")
@@ -1172,6 +1173,10 @@ def main(argv=None):
     ap.add_argument("--latency-runs", type=int, default=20, help="N=1: handoffs timed through run_handoff")
     ap.add_argument("--latency-block-tokens", type=int, default=2048, help="N=1: block_tokens of those handoffs")
     ap.add_argument("--cfg4-steps", type=int, default=5, help="N=1: timed steps of the config-4 sub-record")
+    ap.add_argument("--cfg4-tokens", type=int, default=LLAMA["tokens"],
+                    help="N=1: tokens per config-4 request (smaller only for profiling captures)")
+    ap.add_argument("--cfg4-requests", type=int, default=LLAMA["requests"],
+                    help="N=1: config-4 requests per step (fewer only for profiling captures)")
     ap.add_argument("--skip-cfg4", action="store_true", help="N=1: leave out the config-4 sub-record")
     ap.add_argument("--requests", type=int, default=16, help="requests per step (N>1, config 3)")
     ap.add_argument("--request-tokens", type=int, default=32768, help="history tokens per request (N>1, config 3)")
