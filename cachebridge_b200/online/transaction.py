@@ -292,9 +292,10 @@ def commit(transactions: Sequence[HandoffTransaction], *, settle: Callable[[], N
     the request being committed), or from the id other ranks commit at the
     same position, is not ready.
 
-    Round 1 votes (ready per transaction, safe for the rank). Not safe anywhere
-    -> all quarantined. Not ready anywhere -> that transaction is rolled back
-    (its rows freed once). Round 2 votes on the local publication of the rest:
+    The first vote carries ready per transaction and safe for the rank. Not
+    safe anywhere -> all quarantined. Not ready anywhere -> that transaction is
+    rolled back (its rows freed once). The second vote is on the local
+    publication of the rest:
     a publication that failed on any rank leaves the transaction quarantined.
     A vote that raises quarantines every transaction still open. Returns this
     rank's receipts; raises ``TransactionError`` (with the receipts) unless

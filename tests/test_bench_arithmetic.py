@@ -1,5 +1,5 @@
 """The arithmetic bench.py reports beside its timings, checked on the CPU:
-the algorithmic bytes and flops the rooflines divide by, the parity verdict
+the algorithmic bytes and flops the rooflines divide by, the parity decision
 (relative Frobenius error and the max-abs bound of one BF16 ulp beyond the
 reference's own rounding), and the FP32 restatement's BF16-key option, which
 isolates the one rounding step the kernels add to the reference algorithm."""
